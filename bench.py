@@ -1,0 +1,459 @@
+"""Selective-scan fwd+bwd throughput on B200 (B*D*L Gelem/s) — the metric of
+BASELINE.json.
+
+Default workload: configs[1] — B=8, D=1536, L=2048, N=16, fp32, fused
+softplus(delta + bias), D skip and silu(z) gate, dy ~ N(0,1). One step = one
+forward + one backward of the fused selective scan over one batch (plus, for
+N>1 GPUs, the all-reduce of dA, dD and ddelta_bias across ranks: the batch is
+sharded, each rank holds a full configs[1] batch, i.e. weak scaling).
+``--config c2`` runs configs[2] (bf16 I/O, B=16, D=5120, L=4096, right-padded
+valid lengths ~ U[512, 4096]).
+
+``--impl reference`` times the reference's CPU path instead: JAX is not
+installed on this image, so it runs the NumPy restatement of the reference's
+math from oracle/ (forward + analytic backward) on all host cores, on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "jax-mambas_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "selective-scan fwd+bwd B*D*L elements/s"
+UNIT = "Gelem/s"
+
+CONFIGS = {
+    "c1": dict(workload="configs[1]: fused selective scan fwd+bwd, Mamba-130M layer shape",
+               batch=8, dim=1536, length=2048, dstate=16, dtype="f32", padded=False),
+    "c2": dict(workload="configs[2]: fused selective scan fwd+bwd, Mamba-2.8B layer shape, "
+                        "bf16 I/O, right padding",
+               batch=16, dim=5120, length=4096, dstate=16, dtype="bf16", padded=True),
+}
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), float(j.get("sm_max_mhz", 1965.0)), "measured"
+    return 6650.0, 1965.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[2] > 250.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3])
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded),
+                "sm_max_mhz": max(r[1] for r in rows), "samples": len(loaded),
+                "reasons": reasons}
+
+
+# ---------------------------------------------------------------- GPU arm
+def _algorithmic(cfg, esize):
+    b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+    elems = b * d * L
+    bnl = b * n * L
+    nch = math.ceil(L / 256)
+    cs = b * d * nch * n * 4
+    fwd = elems * 4 * esize + 2 * bnl * esize + cs          # u, delta, z in; out; B, C; carries
+    bwd = elems * 7 * esize + 4 * bnl * esize + cs          # u, delta, z, dy in; du, ddelta, dz out
+    # special-function-unit ops per element: N ex2 per pass, plus softplus
+    # (exp, log), sigmoid(z) (exp, rcp) in the forward and softplus, sigmoid
+    # of delta and sigmoid(z) in the backward
+    mufu_fwd = n + 4
+    mufu_bwd = n + 6
+    return elems, fwd, bwd, mufu_fwd, mufu_bwd
+
+
+def run_gpu(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    from mamba import selective_scan_cuda as ssc
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+    io = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    esize = 2 if io == torch.bfloat16 else 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    def normal(*shape):
+        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(io)
+
+    u, delta, z, dout = normal(b, d, L), normal(b, d, L), normal(b, d, L), normal(b, d, L)
+    Bm, Cm = normal(b, n, L), normal(b, n, L)
+    A = (-torch.arange(1, n + 1, device=dev, dtype=torch.float32)).expand(d, n).contiguous()
+    Dp = torch.randn(d, generator=g, device=dev)
+    bias = torch.rand(d, generator=g, device=dev) * 2.0 - 4.0
+    seq_lens = None
+    if cfg["padded"]:
+        seq_lens = torch.randint(512, L + 1, (b,), generator=g, device=dev, dtype=torch.int32)
+        t_idx = torch.arange(L, device=dev)
+        m = (t_idx[None, :] < seq_lens[:, None].long())[:, None, :]
+        delta.masked_fill_(~m, 0)
+        u.masked_fill_(~m, 0)
+
+    out = torch.empty_like(u)
+    last = torch.empty(b, d, n, device=dev)
+    cs = torch.empty(ssc.chunk_states_elems(b, L, d, n), device=dev)
+    du, ddl, dz = torch.empty_like(u), torch.empty_like(u), torch.empty_like(u)
+    dB, dC = torch.empty_like(Bm), torch.empty_like(Cm)
+    params = torch.empty(d * n + 2 * d, device=dev)  # dA | dD | dbias (one all-reduce)
+    dA, dDp, dbias = params[: d * n].view(d, n), params[d * n: d * n + d], params[d * n + d:]
+    ws = ssc._alloc_workspace(b, L, d, n, 1 if io == torch.bfloat16 else 0, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fwd():
+        ssc.fused_forward_into(u, delta, A, Bm, Cm, Dp, z, bias, True, None, seq_lens,
+                               out, last, cs)
+
+    def bwd():
+        ssc.fused_backward_into(u, delta, A, Bm, Cm, Dp, z, bias, True, None, seq_lens, cs,
+                                dout, None, du, ddl, dA, dB, dC, dDp, dz, dbias, None, ws)
+
+    def step():
+        fwd()
+        bwd()
+        if world > 1:
+            dist.all_reduce(params)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            fwd()
+            ev[i][1].record(stream)
+            bwd()
+            ev[i][2].record(stream)
+            if world > 1:
+                dist.all_reduce(params)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    clocks = sampler.summary()
+
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+
+    elems, fwd_bytes, bwd_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize)
+    ms_per_step = total_ms / args.steps
+    value = elems * world / (ms_per_step * 1e-3) / 1e9
+
+    # ---- e2e through the public API with host buffers
+    e2e = run_e2e(args, cfg, dev, io, rank, world) if args.e2e else None
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return None
+
+    hbm, sm_max, peak_src = _peaks()
+    bwd_gbs = bwd_bytes / (bwd_ms * 1e-3) / 1e9
+    fwd_gbs = fwd_bytes / (fwd_ms * 1e-3) / 1e9
+    f_mhz = clocks.get("sm_mhz") or sm_max
+    mufu_peak = 148 * 16 * f_mhz * 1e6  # ops/s: 16 MUFU lanes per SM per clock
+    mufu_bwd = elems * mufu_b / (bwd_ms * 1e-3)
+    mufu_fwd = elems * mufu_f / (fwd_ms * 1e-3)
+    res = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1)/U(-4,-2) inputs of the config)",
+        "config": {"workload": cfg["workload"], "batch_per_gpu": b, "dim": d, "length": L,
+                   "dstate": n, "global_batch": b * world,
+                   "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (u, delta, z, dy: "
+                         f"{elems * esize * 4 / 1e6:.0f} MB per step)"},
+        "kernels_ms": {"fwd": round(fwd_ms, 4), "bwd": round(bwd_ms, 4)},
+        "roofline": {"bound": "hbm", "kernel": "ss_bwd_kernel",
+                     "achieved": round(bwd_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(bwd_gbs / hbm, 4), "traffic": args.traffic,
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_src == "measured" else "fallback 6.65 TB/s",
+                     "algorithmic_bytes_per_launch": bwd_bytes},
+        "roofline_fwd": {"bound": "hbm", "kernel": "ss_fwd_kernel", "achieved": round(fwd_gbs, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(fwd_gbs / hbm, 4)},
+        "roofline_sfu": {"bound": "sfu", "unit": "MUFU op/s",
+                         "peak": mufu_peak, "clock_mhz": f_mhz,
+                         "bwd_frac": round(mufu_bwd / mufu_peak, 4),
+                         "fwd_frac": round(mufu_fwd / mufu_peak, 4),
+                         "ops_per_elem": {"fwd": mufu_f, "bwd": mufu_b}},
+        "clocks": clocks,
+        "gpu_launches": args.steps * (3 if io == torch.float32 else 5),
+    }
+    if e2e is not None:
+        res["e2e"] = e2e
+    if args.cpu_baseline and world == 1:
+        res["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return res
+
+
+def run_e2e(args, cfg, dev, io, rank, world):
+    """Same metric through selective_scan_fn + autograd with pinned host
+    inputs copied in and all results copied out every step."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba.selective_scan_cuda import selective_scan_fn
+
+    b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+    g = torch.Generator()
+    g.manual_seed(99 + rank)
+
+    def host(*shape):
+        return torch.randn(*shape, generator=g).to(io).pin_memory()
+
+    h = {"u": host(b, d, L), "delta": host(b, d, L), "z": host(b, d, L),
+         "dout": host(b, d, L), "B": host(b, n, L), "C": host(b, n, L)}
+    hA = (-torch.arange(1, n + 1, dtype=torch.float32)).expand(d, n).contiguous().pin_memory()
+    hD = torch.randn(d, generator=g).pin_memory()
+    hb = (torch.rand(d, generator=g) * 2 - 4).pin_memory()
+    hseq = None
+    if cfg["padded"]:
+        hseq = torch.randint(512, L + 1, (b,), generator=g, dtype=torch.int32).pin_memory()
+    outs = {k: torch.empty((b, d, L), dtype=io).pin_memory() for k in ("out", "du", "ddelta", "dz")}
+    outs.update({k: torch.empty((b, n, L), dtype=io).pin_memory() for k in ("dB", "dC")})
+    outs["dA"] = torch.empty(d, n).pin_memory()
+    outs["dD"] = torch.empty(d).pin_memory()
+    outs["dbias"] = torch.empty(d).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in list(h.values()) + [hA, hD, hb])
+    d2h = sum(t.numel() * t.element_size() for t in outs.values())
+
+    def step():
+        t = {k: v.to(dev, non_blocking=True) for k, v in h.items()}
+        A = hA.to(dev, non_blocking=True).requires_grad_(True)
+        Dp = hD.to(dev, non_blocking=True).requires_grad_(True)
+        bias = hb.to(dev, non_blocking=True).requires_grad_(True)
+        seq = hseq.to(dev, non_blocking=True) if hseq is not None else None
+        for k in ("u", "delta", "z", "B", "C"):
+            t[k].requires_grad_(True)
+        out = selective_scan_fn(t["u"], t["delta"], A, t["B"], t["C"], Dp, t["z"], bias,
+                                delta_softplus=True, seq_lens=seq)
+        out.backward(t["dout"])
+        if world > 1:
+            flat = torch.cat([A.grad.flatten(), Dp.grad, bias.grad])
+            dist.all_reduce(flat)
+        outs["out"].copy_(out.detach(), non_blocking=True)
+        outs["du"].copy_(t["u"].grad, non_blocking=True)
+        outs["ddelta"].copy_(t["delta"].grad, non_blocking=True)
+        outs["dz"].copy_(t["z"].grad, non_blocking=True)
+        outs["dB"].copy_(t["B"].grad, non_blocking=True)
+        outs["dC"].copy_(t["C"].grad, non_blocking=True)
+        outs["dA"].copy_(A.grad, non_blocking=True)
+        outs["dD"].copy_(Dp.grad, non_blocking=True)
+        outs["dbias"].copy_(bias.grad, non_blocking=True)
+
+    for _ in range(max(1, min(args.warmup, 3))):
+        step()
+    torch.cuda.synchronize()
+    k = max(1, min(args.steps, 10))
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    s.record()
+    for _ in range(k):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / k
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = b * d * L * world / (ms * 1e-3) / 1e9
+    return {"value": round(value, 3), "unit": UNIT, "ms_per_step": round(ms, 3),
+            "steps": k, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "mamba.selective_scan_cuda.selective_scan_fn + autograd backward"}
+
+
+# ---------------------------------------------------------------- CPU arm
+def _cpu_sample_shape(cfg, seconds_target):
+    # a bounded sample: full length and state size, a slice of the channels
+    return 1, 128 * max(1, os.cpu_count() or 1), cfg["length"], cfg["dstate"]
+
+
+def _cpu_slice(job):
+    """One process' share of the CPU sample: channels [lo, hi) of a seeded case."""
+    b, d, L, n, lo, hi = job
+    import numpy as np
+
+    from oracle import selective_scan_oracle as orc
+
+    x = orc.make_inputs(b, hi - lo, L, n, seed=5 + lo, dtype=np.float32)
+    t0 = time.perf_counter()
+    orc.fused_backward(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"],
+                       x["delta_bias"], True, None, True, None, dout=x["dout"],
+                       dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def _cpu_run(cfg, b, d, L, n, workers):
+    """Wall time of the oracle port over a (b, d, L, n) sample split by
+    channels across `workers` processes (inputs are generated in each worker
+    before its clock starts; the slowest worker's time is returned)."""
+    import multiprocessing as mp
+
+    per = max(1, d // workers)
+    jobs = [(b, d, L, n, i, min(d, i + per)) for i in range(0, d, per)]
+    with mp.get_context("fork").Pool(workers) as pool:
+        times = pool.map(_cpu_slice, jobs)
+    return max(times)
+
+
+def cpu_baseline(cfg, seconds=15.0):
+    """Oracle port (NumPy forward + analytic backward, fp32) on a bounded
+    sample: one sequence of the config's length and state size, a slice of its
+    channels, split across host threads."""
+    threads = os.cpu_count() or 1
+    b, d, L, n = _cpu_sample_shape(cfg, seconds)
+    dt = _cpu_run(cfg, b, d, L, n, threads)
+    return {"value": round(b * d * L / dt / 1e9, 6), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"B={b} D={d} L={L} N={n} (of B={cfg['batch']} D={cfg['dim']}), fp32, "
+                      f"{dt:.2f} s, NumPy restatement of the reference math "
+                      "(fwd + analytic bwd); JAX absent on this image"}
+
+
+def run_reference(args, cfg):
+    """--impl reference: the reference's CPU path (its NumPy restatement)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    b, d, L, n = _cpu_sample_shape(cfg, args.cpu_seconds)
+    for _ in range(max(0, min(args.warmup, 1))):
+        _cpu_run(cfg, b, d, min(L, 256), n, threads)
+    times = [_cpu_run(cfg, b, d, L, n, threads) for _ in range(max(1, min(args.steps, 3)))]
+    dt = statistics.mean(times)
+    value = b * d * L / dt / 1e9
+    res = {"metric": METRIC, "value": round(value, 6), "unit": UNIT, "impl": "reference",
+           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(times),
+           "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": cfg["workload"], "batch": cfg["batch"], "dim": cfg["dim"],
+                      "length": cfg["length"], "dstate": cfg["dstate"]},
+           "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads,
+                            "kind": "port",
+                            "sample": f"each step B={b} D={d} L={L} N={n}; NumPy restatement "
+                                      "of the reference's pure-JAX math (JAX not installed)"},
+           "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--no-e2e", dest="e2e", action="store_false")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu dram bytes per backward launch, if captured")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_gpu(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,137 @@
+/*
+ * C ABI of the B200 (sm_100a) Mamba-1 selective scan.
+ *
+ * These entry points replace the XLA typed-FFI handlers of the JAX-Mambas
+ * reference (MambaSelectiveScan, MambaSelectiveScanBackward and
+ * MambaSelectiveScanBenchmark in native/selective_scan_cuda.cu and
+ * native/selective_scan_bwd.cu). Arguments are plain device pointers, sizes
+ * and a cudaStream_t passed as void*; nothing here allocates device memory or
+ * synchronises the host. Every function returns an mss_status; on failure
+ * mamba_ss_last_error() gives a message for the calling host thread.
+ *
+ * Physical layouts (row-major, last index fastest):
+ *   u, delta, z, y / out, du, ddelta, dz, dy ... (batch, dim, length)
+ *   B, C, dB, dC ............................... (batch, dstate, length)
+ *   A, dA ...................................... (dim, dstate)        fp32
+ *   D, delta_bias, dD, ddelta_bias ............. (dim)                fp32
+ *   initial_state, last_state, d_* ............. (batch, dim, dstate) fp32
+ *   chunk_states ............................... (batch, dim, n_chunks, dstate) fp32
+ *   seq_lens ................................... (batch) int32
+ * These are the physical layouts the reference pins through its ffi_call
+ * input_layouts/output_layouts (mamba/selective_scan_cuda.py:138-146,180-198).
+ */
+#ifndef MAMBA_SELECTIVE_SCAN_H_
+#define MAMBA_SELECTIVE_SCAN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MSS_OK = 0,
+  MSS_INVALID_ARGUMENT = 1, /* like ffi::Error::InvalidArgument, cu:402-440 */
+  MSS_INTERNAL = 2          /* like ffi::Error::Internal, cu:334-337 */
+} mss_status;
+
+typedef enum { MSS_F32 = 0, MSS_BF16 = 1 } mss_dtype;
+
+typedef enum { MSS_EULER = 0, MSS_ZOH = 1 } mss_discretization;
+
+/* Time steps covered by one saved carry (one entry of chunk_states). */
+#define MSS_CHUNK 256
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* mamba_ss_last_error(void);
+
+/* Library version string, e.g. "mamba-ss-b200 0.1 sm_100a". */
+const char* mamba_ss_version(void);
+
+/* Number of fp32 elements of chunk_states: batch*dim*ceil(length/256)*dstate.
+ * The reference sizes the same residual (batch, dim, ceil(L/2048), N, 2)
+ * (mamba/selective_scan_cuda.py:129-134); it is private to the custom_vjp. */
+int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
+                                    int32_t dstate);
+
+/* ---------------------------------------------------------------------------
+ * Reference contract (fp32, no D / z / bias / softplus in the kernel).
+ * ------------------------------------------------------------------------- */
+
+/* Replaces MambaSelectiveScan (native/selective_scan_cuda.cu:554-573):
+ * attrs discretization, batch, length, dim, dstate; args A, deltas, B, C, u,
+ * initial_x; rets y, final_x, chunk_states. */
+mss_status mamba_ss_fwd(void* stream, int32_t discretization, int32_t batch,
+                        int32_t length, int32_t dim, int32_t dstate,
+                        const float* A, const float* deltas, const float* B,
+                        const float* C, const float* u, const float* initial_x,
+                        float* y, float* final_x, float* chunk_states);
+
+/* Replaces MambaSelectiveScanBenchmark (native/selective_scan_cuda.cu:578-598):
+ * the forward launched `repeats` times behind one call. */
+mss_status mamba_ss_fwd_bench(void* stream, int32_t discretization,
+                              int32_t repeats, int32_t batch, int32_t length,
+                              int32_t dim, int32_t dstate, const float* A,
+                              const float* deltas, const float* B,
+                              const float* C, const float* u,
+                              const float* initial_x, float* y, float* final_x,
+                              float* chunk_states);
+
+/* Bytes of caller-provided scratch the backward needs (both contracts). */
+size_t mamba_ss_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
+                                    int32_t dstate, int32_t io_dtype);
+
+/* Replaces MambaSelectiveScanBackward (native/selective_scan_bwd.cu:166-190):
+ * attrs batch, length, dim, dstate; args A, deltas, B, C, u, initial_x,
+ * chunk_states, dy, dfinal_x; rets dA, ddeltas, dB, dC, du, dinitial_x.
+ * The reference backward is Euler-only and falls back to JAX autodiff for
+ * ZOH (mamba/selective_scan_cuda.py:236-256); this one takes discretization
+ * as well. workspace must hold mamba_ss_bwd_workspace_bytes(...,MSS_F32). */
+mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
+                        int32_t length, int32_t dim, int32_t dstate,
+                        const float* A, const float* deltas, const float* B,
+                        const float* C, const float* u, const float* initial_x,
+                        const float* chunk_states, const float* dy,
+                        const float* dfinal_x, float* dA, float* ddeltas,
+                        float* dB, float* dC, float* du, float* dinitial_x,
+                        void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Fused contract: selective_scan(u, delta, A, B, C, D, z, delta_bias,
+ * delta_softplus, return_last_state) of the north-star signature, plus
+ * initial_state, discretization and per-sequence valid lengths.
+ *   delta_eff = softplus(delta + delta_bias)  (softplus if delta_softplus)
+ *   h_t = exp(delta_eff*A) h_{t-1} + delta_eff*B_t*u_t          (Euler)
+ *   out = (sum_n C_t h_t + D*u) * silu(z)
+ * Optional pointers (D, z, delta_bias, initial_state, seq_lens, last_state,
+ * dfinal_state and their gradients) may be NULL. With seq_lens, steps
+ * t >= seq_lens[b] are padding: their delta and u count as 0, their output
+ * and input gradients are written as exact zeros.
+ * io_dtype (MSS_F32 or MSS_BF16) types u, delta, z, B, C, out and their
+ * gradients; the state, A, D, delta_bias and reductions stay fp32.
+ * ------------------------------------------------------------------------- */
+mss_status mamba_ss_fused_fwd(
+    void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,
+    int32_t length, int32_t dim, int32_t dstate, const void* u,
+    const void* delta, const float* A, const void* B, const void* C,
+    const float* D, const void* z, const float* delta_bias,
+    int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
+    void* out, float* last_state, float* chunk_states);
+
+mss_status mamba_ss_fused_bwd(
+    void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,
+    int32_t length, int32_t dim, int32_t dstate, const void* u,
+    const void* delta, const float* A, const void* B, const void* C,
+    const float* D, const void* z, const float* delta_bias,
+    int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
+    const float* chunk_states, const void* dout, const float* dlast_state,
+    void* du, void* ddelta, float* dA, void* dB, void* dC, float* dD,
+    void* dz, float* ddelta_bias, float* dinitial_state, void* workspace,
+    size_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA_SELECTIVE_SCAN_H_ */

@@ -1,0 +1,254 @@
+// extern "C" entry points of libmamba_ss_b200.so (declared in
+// include/mamba_selective_scan.h). They validate arguments the way the
+// reference's FFI handlers do (native/selective_scan_cuda.cu:400-440,
+// native/selective_scan_bwd.cu:45-79), launch on the caller's stream and
+// report errors through a status code plus a per-thread message.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "ss_launch.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+mss_status fail(mss_status code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+mss_status cuda_fail(const char* what, cudaError_t e) {
+  return fail(MSS_INTERNAL, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool valid_dstate(int n) {
+  return n == 1 || n == 2 || n == 4 || n == 8 || n == 16;
+}
+
+mss_status check_dims(const char* op, int io_dtype, int discretization,
+                      int batch, int length, int dim, int dstate) {
+  if (batch <= 0 || length <= 0 || dim <= 0)
+    return fail(MSS_INVALID_ARGUMENT,
+                std::string(op) + ": selective scan dimensions must be positive");
+  if (!valid_dstate(dstate))
+    return fail(MSS_INVALID_ARGUMENT,
+                std::string(op) + ": N must be one of 1, 2, 4, 8, or 16");
+  if (discretization != MSS_EULER && discretization != MSS_ZOH)
+    return fail(MSS_INVALID_ARGUMENT,
+                std::string(op) + ": discretization must be 0 (Euler) or 1 (ZOH)");
+  if (io_dtype != MSS_F32 && io_dtype != MSS_BF16)
+    return fail(MSS_INVALID_ARGUMENT,
+                std::string(op) + ": io_dtype must be 0 (f32) or 1 (bf16)");
+  if (static_cast<int64_t>(batch) * dim > (1ll << 31) / 1 ||
+      static_cast<int64_t>(dim) * dstate > (1ll << 31))
+    return fail(MSS_INVALID_ARGUMENT, std::string(op) + ": sizes too large");
+  return MSS_OK;
+}
+
+int n_chunks_of(int length) { return (length + mss::kChunk - 1) / mss::kChunk; }
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct BwdWorkspace {
+  size_t dA_part, dD_part, dbias_part, dB_acc, dC_acc, total;
+};
+
+BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
+                        int io_dtype) {
+  BwdWorkspace w{};
+  size_t off = 0;
+  w.dA_part = off;
+  off += align256(sizeof(float) * static_cast<size_t>(batch) * dim * dstate);
+  w.dD_part = off;
+  off += align256(sizeof(float) * static_cast<size_t>(batch) * dim);
+  w.dbias_part = off;
+  off += align256(sizeof(float) * static_cast<size_t>(batch) * dim);
+  w.dB_acc = w.dC_acc = 0;
+  if (io_dtype == MSS_BF16) {
+    const size_t bnl =
+        align256(sizeof(float) * static_cast<size_t>(batch) * dstate * length);
+    w.dB_acc = off;
+    off += bnl;
+    w.dC_acc = off;
+    off += bnl;
+  }
+  w.total = off;
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mamba_ss_last_error(void) { return g_last_error.c_str(); }
+
+const char* mamba_ss_version(void) { return "mamba-ss-b200 0.1 sm_100a"; }
+
+int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
+                                    int32_t dstate) {
+  if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
+  return static_cast<int64_t>(batch) * dim * n_chunks_of(length) * dstate;
+}
+
+size_t mamba_ss_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
+                                    int32_t dstate, int32_t io_dtype) {
+  if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
+  return bwd_layout(batch, length, dim, dstate, io_dtype).total;
+}
+
+mss_status mamba_ss_fused_fwd(
+    void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,
+    int32_t length, int32_t dim, int32_t dstate, const void* u,
+    const void* delta, const float* A, const void* B, const void* C,
+    const float* D, const void* z, const float* delta_bias,
+    int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
+    void* out, float* last_state, float* chunk_states) {
+  mss_status st = check_dims("mamba_ss_fused_fwd", io_dtype, discretization,
+                             batch, length, dim, dstate);
+  if (st != MSS_OK) return st;
+  if (!u || !delta || !A || !B || !C || !out || !chunk_states)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_fused_fwd: u, delta, A, B, C, out and chunk_states "
+                "must be non-null");
+  mss::FwdParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.seqlen = length;
+  p.n_chunks = n_chunks_of(length);
+  p.delta_softplus = delta_softplus ? 1 : 0;
+  p.u = u;
+  p.delta = delta;
+  p.z = z;
+  p.B = B;
+  p.C = C;
+  p.A = A;
+  p.D = D;
+  p.delta_bias = delta_bias;
+  p.h0 = initial_state;
+  p.seq_lens = seq_lens;
+  p.out = out;
+  p.last_state = last_state;
+  p.chunk_states = chunk_states;
+  cudaError_t e = mss::launch_fwd(p, dstate, io_dtype, discretization,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching selective scan forward", e);
+  return MSS_OK;
+}
+
+mss_status mamba_ss_fused_bwd(
+    void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,
+    int32_t length, int32_t dim, int32_t dstate, const void* u,
+    const void* delta, const float* A, const void* B, const void* C,
+    const float* D, const void* z, const float* delta_bias,
+    int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
+    const float* chunk_states, const void* dout, const float* dlast_state,
+    void* du, void* ddelta, float* dA, void* dB, void* dC, float* dD,
+    void* dz, float* ddelta_bias, float* dinitial_state, void* workspace,
+    size_t workspace_bytes) {
+  mss_status st = check_dims("mamba_ss_fused_bwd", io_dtype, discretization,
+                             batch, length, dim, dstate);
+  if (st != MSS_OK) return st;
+  if (!u || !delta || !A || !B || !C || !chunk_states || !dout || !du ||
+      !ddelta || !dA || !dB || !dC)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_fused_bwd: u, delta, A, B, C, chunk_states, dout, du, "
+                "ddelta, dA, dB and dC must be non-null");
+  if (z && !dz)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_bwd: z given without dz");
+  const BwdWorkspace w = bwd_layout(batch, length, dim, dstate, io_dtype);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_fused_bwd: workspace needs " + std::to_string(w.total) +
+                    " bytes, got " + std::to_string(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_fused_bwd: workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  mss::BwdParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.seqlen = length;
+  p.n_chunks = n_chunks_of(length);
+  p.delta_softplus = delta_softplus ? 1 : 0;
+  p.u = u;
+  p.delta = delta;
+  p.z = z;
+  p.B = B;
+  p.C = C;
+  p.A = A;
+  p.D = D;
+  p.delta_bias = delta_bias;
+  p.h0 = initial_state;
+  p.seq_lens = seq_lens;
+  p.chunk_states = chunk_states;
+  p.dout = dout;
+  p.dlast = dlast_state;
+  p.du = du;
+  p.ddelta = ddelta;
+  p.dz = z ? dz : nullptr;
+  p.dA_part = reinterpret_cast<float*>(ws + w.dA_part);
+  p.dD_part = reinterpret_cast<float*>(ws + w.dD_part);
+  p.dbias_part = reinterpret_cast<float*>(ws + w.dbias_part);
+  if (io_dtype == MSS_BF16) {
+    p.dB_acc = reinterpret_cast<float*>(ws + w.dB_acc);
+    p.dC_acc = reinterpret_cast<float*>(ws + w.dC_acc);
+  } else {
+    p.dB_acc = static_cast<float*>(dB);
+    p.dC_acc = static_cast<float*>(dC);
+  }
+  p.dh0 = dinitial_state;
+  cudaError_t e = mss::launch_bwd(p, dstate, io_dtype, discretization, dB, dC,
+                                  dA, D ? dD : nullptr,
+                                  delta_bias ? ddelta_bias : nullptr,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching selective scan backward", e);
+  return MSS_OK;
+}
+
+mss_status mamba_ss_fwd(void* stream, int32_t discretization, int32_t batch,
+                        int32_t length, int32_t dim, int32_t dstate,
+                        const float* A, const float* deltas, const float* B,
+                        const float* C, const float* u, const float* initial_x,
+                        float* y, float* final_x, float* chunk_states) {
+  return mamba_ss_fused_fwd(stream, MSS_F32, discretization, batch, length, dim,
+                            dstate, u, deltas, A, B, C, nullptr, nullptr,
+                            nullptr, 0, initial_x, nullptr, y, final_x,
+                            chunk_states);
+}
+
+mss_status mamba_ss_fwd_bench(void* stream, int32_t discretization,
+                              int32_t repeats, int32_t batch, int32_t length,
+                              int32_t dim, int32_t dstate, const float* A,
+                              const float* deltas, const float* B,
+                              const float* C, const float* u,
+                              const float* initial_x, float* y, float* final_x,
+                              float* chunk_states) {
+  if (repeats <= 0)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fwd_bench: repeats must be positive");
+  for (int r = 0; r < repeats; ++r) {
+    mss_status st = mamba_ss_fwd(stream, discretization, batch, length, dim,
+                                 dstate, A, deltas, B, C, u, initial_x, y,
+                                 final_x, chunk_states);
+    if (st != MSS_OK) return st;
+  }
+  return MSS_OK;
+}
+
+mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
+                        int32_t length, int32_t dim, int32_t dstate,
+                        const float* A, const float* deltas, const float* B,
+                        const float* C, const float* u, const float* initial_x,
+                        const float* chunk_states, const float* dy,
+                        const float* dfinal_x, float* dA, float* ddeltas,
+                        float* dB, float* dC, float* du, float* dinitial_x,
+                        void* workspace, size_t workspace_bytes) {
+  return mamba_ss_fused_bwd(stream, MSS_F32, discretization, batch, length, dim,
+                            dstate, u, deltas, A, B, C, nullptr, nullptr,
+                            nullptr, 0, initial_x, nullptr, chunk_states, dy,
+                            dfinal_x, du, ddeltas, dA, dB, dC, nullptr, nullptr,
+                            nullptr, dinitial_x, workspace, workspace_bytes);
+}
+
+}  // extern "C"

@@ -1,0 +1,219 @@
+// Shared device code of the sm_100a selective scan: parameter blocks, typed
+// row loads/stores and the per-element activation helpers.
+//
+// Work decomposition (forward and backward):
+//   * one warp owns one (batch, channel) row and walks L in chunks of
+//     MSS_CHUNK = 32 lanes x kItems steps;
+//   * lane i owns the kItems consecutive steps [t0 + i*kItems, ...) of a chunk;
+//   * the recurrence h_t = a_t h_{t-1} + b_t runs per state in fp32 registers:
+//     a lane-local pass, a warp-shuffle scan of the (prod a, h) pairs over the
+//     32 lanes, then a lane-local re-scan seeded with the lane's prefix;
+//   * the carry across chunks is kept per state in registers (forward) or in
+//     shared memory (backward).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mamba_selective_scan.h"
+
+namespace mss {
+
+constexpr int kItems = 8;                   // steps per lane per chunk
+constexpr int kChunk = 32 * kItems;         // steps per chunk (== MSS_CHUNK)
+static_assert(kChunk == MSS_CHUNK, "chunk size must match the public header");
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct FwdParams {
+  int batch, dim, seqlen, n_chunks;
+  int delta_softplus;
+  const void* u;
+  const void* delta;
+  const void* z;
+  const void* B;
+  const void* C;
+  const float* A;
+  const float* D;
+  const float* delta_bias;
+  const float* h0;
+  const int32_t* seq_lens;
+  void* out;
+  float* last_state;
+  float* chunk_states;
+};
+
+struct BwdParams {
+  int batch, dim, seqlen, n_chunks;
+  int delta_softplus;
+  const void* u;
+  const void* delta;
+  const void* z;
+  const void* B;
+  const void* C;
+  const float* A;
+  const float* D;
+  const float* delta_bias;
+  const float* h0;
+  const int32_t* seq_lens;
+  const float* chunk_states;
+  const void* dout;
+  const float* dlast;
+  void* du;
+  void* ddelta;
+  void* dz;
+  float* dB_acc;   // fp32 (batch, dstate, L), zeroed before the launch
+  float* dC_acc;
+  float* dA_part;  // fp32 (batch, dim, dstate): per-batch partial sums
+  float* dD_part;  // fp32 (batch, dim)
+  float* dbias_part;
+  float* dh0;
+};
+
+// ---------------------------------------------------------------- typed I/O
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ float ld(const float* p) { return __ldg(p); }
+  static __device__ __forceinline__ void st(float* p, float v) { *p = v; }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float ld(const __nv_bfloat16* p) {
+    return __bfloat162float(__ldg(p));
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, float v) {
+    *p = __float2bfloat16_rn(v);
+  }
+};
+
+// Loads kItems consecutive elements row[t .. t+kItems) as fp32; elements at or
+// beyond `limit` read as 0. Uses 16-byte loads when the run is whole and
+// 16-byte aligned.
+template <typename T>
+__device__ __forceinline__ void load_run(const T* row, int t, int limit,
+                                         float (&v)[kItems]) {
+  const T* p = row + t;
+  const bool whole = t + kItems <= limit;
+  if (whole && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+    if constexpr (sizeof(T) == 4) {
+      const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+      for (int j = 0; j < kItems / 4; ++j) {
+        float4 f = __ldg(q + j);
+        v[4 * j + 0] = f.x;
+        v[4 * j + 1] = f.y;
+        v[4 * j + 2] = f.z;
+        v[4 * j + 3] = f.w;
+      }
+    } else {
+      static_assert(kItems % 8 == 0, "bf16 runs load 8 elements per 16 bytes");
+      const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+      for (int j = 0; j < kItems / 8; ++j) {
+        uint4 w = __ldg(q + j);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __bfloat1622float2(h[e]);
+          v[8 * j + 2 * e] = f.x;
+          v[8 * j + 2 * e + 1] = f.y;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k)
+      v[k] = (t + k < limit) ? Elem<T>::ld(p + k) : 0.f;
+  }
+}
+
+// Stores v[0 .. kItems) to row[t ..); elements at or beyond `limit` are not
+// written.
+template <typename T>
+__device__ __forceinline__ void store_run(T* row, int t, int limit,
+                                          const float (&v)[kItems]) {
+  T* p = row + t;
+  const bool whole = t + kItems <= limit;
+  if (whole && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+    if constexpr (sizeof(T) == 4) {
+      float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+      for (int j = 0; j < kItems / 4; ++j)
+        q[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+      for (int j = 0; j < kItems / 8; ++j) {
+        uint4 w;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+        q[j] = w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k)
+      if (t + k < limit) Elem<T>::st(p + k, v[k]);
+  }
+}
+
+// ------------------------------------------------------------- activations
+// 2^x on the special-function unit.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// softplus(x) = log(1 + e^x), the function jax.nn.softplus evaluates
+// (mamba/mamba1.py:76,165); large x pass through unchanged.
+__device__ __forceinline__ float softplus(float x) {
+  return x <= 20.f ? log1pf(expf(x)) : x;
+}
+
+__device__ __forceinline__ float sigmoid(float x) {
+  return 1.f / (1.f + expf(-x));
+}
+
+// ------------------------------------------------------------ warp scans
+// Inclusive scan over lanes of the affine maps h -> P h + H, composed left
+// to right: lane i ends with the composition of lanes 0..i.
+__device__ __forceinline__ void warp_scan_fwd(float& P, float& H, int lane) {
+#pragma unroll
+  for (int s = 1; s < 32; s <<= 1) {
+    const float Pp = __shfl_up_sync(0xffffffffu, P, s);
+    const float Hp = __shfl_up_sync(0xffffffffu, H, s);
+    if (lane >= s) {
+      H = fmaf(P, Hp, H);
+      P *= Pp;
+    }
+  }
+}
+
+// Inclusive scan over lanes of the maps g -> P g + G composed right to left:
+// lane i ends with the composition of lanes i..31.
+__device__ __forceinline__ void warp_scan_rev(float& P, float& G, int lane) {
+#pragma unroll
+  for (int s = 1; s < 32; s <<= 1) {
+    const float Pn = __shfl_down_sync(0xffffffffu, P, s);
+    const float Gn = __shfl_down_sync(0xffffffffu, G, s);
+    if (lane + s < 32) {
+      G = fmaf(P, Gn, G);
+      P *= Pn;
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+  return v;
+}
+
+}  // namespace mss

@@ -1,0 +1,21 @@
+// Host-side launchers shared by the C ABI (ss_capi.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "ss_common.cuh"
+
+namespace mss {
+
+cudaError_t launch_fwd(const FwdParams& p, int dstate, int io_dtype, int zoh,
+                       cudaStream_t stream);
+
+// Runs the backward scan kernel, the batch reduction of the parameter
+// gradients and (bf16 I/O) the fp32 -> bf16 conversion of dB/dC.
+// dB_out/dC_out are the caller's output buffers; p.dB_acc/p.dC_acc are the
+// fp32 accumulators (the outputs themselves for fp32 I/O).
+cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
+                       void* dB_out, void* dC_out, float* dA, float* dD,
+                       float* ddelta_bias, cudaStream_t stream);
+
+}  // namespace mss

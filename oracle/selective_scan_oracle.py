@@ -1,0 +1,280 @@
+"""CPU oracle of the Mamba-1 selective scan — TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module, and only as the checker or the timed CPU
+reference. The product (``jax-mambas_b200/``) never calls it.
+
+It restates, in NumPy, the math of the JAX-Mambas reference:
+
+* ``selective_scan_reference`` follows ``mamba/selective_scan_cuda.py:56-90``
+  (discretise, fold ``initial_x`` into step 0, associative scan with
+  ``compose(l, r) = (r_a*l_a, r_a*l_h + r_h)``, contract with C).
+* ``sequential_recurrence`` follows the known-answer loop of
+  ``tests/test_selective_scan_cuda.py:35-49``.
+* ``fused_forward`` adds the caller-side math of ``S6.__call__`` /
+  ``Mamba.__call__`` (``mamba/mamba1.py:162-198, 308, 332``): softplus of
+  delta (+ bias), padding mask on delta and u (``mamba1.py:167-168``), the D
+  skip and the silu(z) gate, in the (batch, dim, length) layout the kernels use.
+* ``fused_backward`` is the analytic adjoint of ``fused_forward`` (the
+  reference gets it from ``jax.vjp``, ``mamba/selective_scan_cuda.py:255``);
+  the CPU tests pin it against torch.autograd in float64.
+
+Parity pinning: the reference ships no golden vectors and cannot run here
+(JAX is not installed on this image or on the GPU box). The oracle is pinned
+by restating the reference's own known-answer test (associative scan vs
+sequential recurrence, ``tests/test_selective_scan_cuda.py:22-52``) and by
+autograd cross-checks of the backward; see ``tests/test_oracle.py``.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+# --------------------------------------------------------------------------
+# Reference contract: logical layouts u/deltas (B, L, D), Bs/Cs (B, L, N),
+# A (D, N), initial_x (B, D, N).
+# --------------------------------------------------------------------------
+def _associative_scan(a: np.ndarray, h: np.ndarray, axis: int = 1):
+    """Inclusive scan of affine maps along ``axis`` (Hillis-Steele doubling).
+
+    Element i after the scan is compose(e_0, ..., e_i) with
+    compose(left, right) = (right_a * left_a, right_a * left_h + right_h),
+    the operator of ``mamba/selective_scan_cuda.py:83-86``.
+    """
+    a = np.moveaxis(a, axis, 0).copy()
+    h = np.moveaxis(h, axis, 0).copy()
+    n = a.shape[0]
+    s = 1
+    while s < n:
+        a_new = a.copy()
+        h_new = h.copy()
+        a_new[s:] = a[s:] * a[:-s]
+        h_new[s:] = a[s:] * h[:-s] + h[s:]
+        a, h = a_new, h_new
+        s *= 2
+    return np.moveaxis(a, 0, axis), np.moveaxis(h, 0, axis)
+
+
+def discretize(A, deltas, Bs, use_euler_barB_approx=True):
+    """a_bar, b_bar of ``mamba/selective_scan_cuda.py:72-79`` (B, L, D, N)."""
+    delta_a = np.einsum("bld,dn->bldn", deltas, A)
+    a_bars = np.exp(delta_a)
+    if use_euler_barB_approx:
+        b_bars = np.einsum("bld,bln->bldn", deltas, Bs)
+    else:
+        b_bars = np.expm1(delta_a) * np.einsum("dn,bln->bldn", np.reciprocal(A), Bs)
+    return a_bars, b_bars
+
+
+def selective_scan_reference(A, deltas, Bs, Cs, u, initial_x=None, *,
+                             use_euler_barB_approx=True, dtype=np.float64):
+    """Restatement of ``selective_scan_reference`` (selective_scan_cuda.py:56-90)."""
+    A, deltas, Bs, Cs, u = (np.asarray(x, dtype=dtype) for x in (A, deltas, Bs, Cs, u))
+    if initial_x is None:
+        initial_x = np.zeros((u.shape[0], u.shape[2], A.shape[1]), dtype=dtype)
+    initial_x = np.asarray(initial_x, dtype=dtype)
+    a_bars, b_bars = discretize(A, deltas, Bs, use_euler_barB_approx)
+    bu = b_bars * u[..., None]
+    bu[:, 0] += a_bars[:, 0] * initial_x
+    _, states = _associative_scan(a_bars, bu, axis=1)
+    y = np.einsum("bln,bldn->bld", Cs, states)
+    return y, states[:, -1]
+
+
+def sequential_recurrence(A, deltas, Bs, Cs, u, initial_x, *,
+                          use_euler_barB_approx=True, dtype=np.float64):
+    """The known-answer loop of ``tests/test_selective_scan_cuda.py:35-49``."""
+    A, deltas, Bs, Cs, u, initial_x = (
+        np.asarray(x, dtype=dtype) for x in (A, deltas, Bs, Cs, u, initial_x))
+    a_bars, b_bars = discretize(A, deltas, Bs, use_euler_barB_approx)
+    state = initial_x
+    outputs = []
+    for step in range(u.shape[1]):
+        state = a_bars[:, step] * state + b_bars[:, step] * u[:, step, :, None]
+        outputs.append(np.einsum("bn,bdn->bd", Cs[:, step], state))
+    return np.stack(outputs, axis=1), state
+
+
+# --------------------------------------------------------------------------
+# Fused contract in kernel layout: u, delta, z, out (B, D, L); B, C (B, N, L);
+# A (D, N); D, delta_bias (D,); initial_state (B, D, N); seq_lens (B,).
+# --------------------------------------------------------------------------
+def _softplus(x):
+    # jax.nn.softplus(x) == logaddexp(x, 0)
+    return np.logaddexp(x, 0.0)
+
+
+def _sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def _prepare(u, delta, A, B, C, D, z, delta_bias, delta_softplus, seq_lens, dtype):
+    f = lambda x: None if x is None else np.asarray(x, dtype=dtype)
+    u, delta, A, B, C, D, z, delta_bias = map(f, (u, delta, A, B, C, D, z, delta_bias))
+    pre = delta + (delta_bias[None, :, None] if delta_bias is not None else 0.0)
+    dlt = _softplus(pre) if delta_softplus else pre
+    batch, _, L = u.shape
+    if seq_lens is not None:
+        mask = (np.arange(L)[None, :] < np.asarray(seq_lens)[:, None]).astype(dtype)
+    else:
+        mask = np.ones((batch, L), dtype=dtype)
+    m = mask[:, None, :]
+    return u * m, dlt * m, pre, A, B, C, D, z, mask
+
+
+def fused_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                  delta_softplus=False, initial_state=None,
+                  use_euler_barB_approx=True, seq_lens=None, dtype=np.float64):
+    """out, last_state of the fused selective scan (sequential, exact order)."""
+    um, dl, _, A, B, C, D, z, mask = _prepare(
+        u, delta, A, B, C, D, z, delta_bias, delta_softplus, seq_lens, dtype)
+    batch, dim, L = um.shape
+    N = A.shape[1]
+    h = (np.zeros((batch, dim, N), dtype=dtype) if initial_state is None
+         else np.asarray(initial_state, dtype=dtype).copy())
+    y = np.empty((batch, dim, L), dtype=dtype)
+    for t in range(L):
+        dA = dl[:, :, t, None] * A[None]
+        a = np.exp(dA)
+        if use_euler_barB_approx:
+            bbar = dl[:, :, t, None] * B[:, None, :, t]
+        else:
+            bbar = np.expm1(dA) / A[None] * B[:, None, :, t]
+        h = a * h + bbar * um[:, :, t, None]
+        y[:, :, t] = np.einsum("bn,bdn->bd", C[:, :, t], h)
+    out = y
+    if D is not None:
+        out = out + D[None, :, None] * um
+    if z is not None:
+        out = out * (z * _sigmoid(z))
+    if seq_lens is not None:
+        out = out * mask[:, None, :]
+    return out, h
+
+
+def fused_backward(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                   delta_softplus=False, initial_state=None,
+                   use_euler_barB_approx=True, seq_lens=None, dout=None,
+                   dlast_state=None, dtype=np.float64):
+    """Gradients of ``fused_forward`` w.r.t. every input.
+
+    Returns a dict with du, ddelta, dA, dB, dC, dD, dz, ddelta_bias,
+    dinitial_state (None where the input is None).
+    """
+    um, dl, pre, A, B, C, D, z, mask = _prepare(
+        u, delta, A, B, C, D, z, delta_bias, delta_softplus, seq_lens, dtype)
+    zero_state = initial_state is None
+    batch, dim, L = um.shape
+    N = A.shape[1]
+    h0 = (np.zeros((batch, dim, N), dtype=dtype) if zero_state
+          else np.asarray(initial_state, dtype=dtype))
+    dout = np.asarray(dout, dtype=dtype) * mask[:, None, :]
+    euler = use_euler_barB_approx
+
+    # forward pass, keeping every state
+    hs = np.empty((L + 1, batch, dim, N), dtype=dtype)
+    hs[0] = h0
+    a_all = np.empty((L, batch, dim, N), dtype=dtype)
+    y = np.empty((batch, dim, L), dtype=dtype)
+    for t in range(L):
+        dA = dl[:, :, t, None] * A[None]
+        a = np.exp(dA)
+        bbar = (dl[:, :, t, None] * B[:, None, :, t] if euler
+                else np.expm1(dA) / A[None] * B[:, None, :, t])
+        hs[t + 1] = a * hs[t] + bbar * um[:, :, t, None]
+        a_all[t] = a
+        y[:, :, t] = np.einsum("bn,bdn->bd", C[:, :, t], hs[t + 1])
+
+    pre_gate = y + (D[None, :, None] * um if D is not None else 0.0)
+    if z is not None:
+        sg = _sigmoid(z)
+        dz = dout * pre_gate * sg * (1.0 + z * (1.0 - sg))
+        dy = dout * z * sg
+    else:
+        dz = None
+        dy = dout
+    dD = np.einsum("bdl,bdl->d", dy, um) if D is not None else None
+
+    g = (np.zeros((batch, dim, N), dtype=dtype) if dlast_state is None
+         else np.asarray(dlast_state, dtype=dtype).copy())
+    d_dl = np.zeros((batch, dim, L), dtype=dtype)
+    d_um = np.zeros((batch, dim, L), dtype=dtype)
+    dA_tot = np.zeros_like(A)
+    dB = np.zeros_like(B)
+    dC = np.zeros_like(C)
+    for t in range(L - 1, -1, -1):
+        g = g + dy[:, :, t, None] * C[:, None, :, t]          # dL/dh_t
+        dC[:, :, t] = np.einsum("bd,bdn->bn", dy[:, :, t], hs[t + 1])
+        a = a_all[t]
+        dt = dl[:, :, t, None]
+        w = g * a * hs[t]                                      # g a h_{t-1}
+        d_dl[:, :, t] += np.einsum("bdn,dn->bd", w, A)
+        dA_tot += np.einsum("bdn,bd->dn", w, dl[:, :, t])
+        ut = um[:, :, t, None]
+        if euler:
+            d_dl[:, :, t] += np.einsum("bdn,bn->bd", g, B[:, :, t]) * um[:, :, t]
+            d_um[:, :, t] += np.einsum("bdn,bn->bd", g, B[:, :, t]) * dl[:, :, t]
+            dB[:, :, t] += np.einsum("bdn,bd->bn", g, dl[:, :, t] * um[:, :, t])
+        else:
+            em1 = np.expm1(dt * A[None])
+            bb = em1 / A[None]
+            Bt = B[:, None, :, t]
+            d_dl[:, :, t] += np.einsum("bdn->bd", g * a * Bt * ut)
+            d_um[:, :, t] += np.einsum("bdn->bd", g * bb * Bt)
+            dB[:, :, t] += np.einsum("bdn->bn", g * bb * ut)
+            dA_tot += np.einsum("bdn->dn", g * Bt * ut * (dt * a / A[None] - em1 / A[None] ** 2))
+        g = g * a                                              # -> dL/dh_{t-1}
+    if D is not None:
+        d_um += D[None, :, None] * dy
+    # masked inputs: the mask multiplies u and the activated delta
+    du = d_um * mask[:, None, :]
+    d_dl = d_dl * mask[:, None, :]
+    ddelta = d_dl * _sigmoid(pre) if delta_softplus else d_dl
+    ddelta_bias = ddelta.sum(axis=(0, 2)) if delta_bias is not None else None
+    return {
+        "du": du,
+        "ddelta": ddelta,
+        "dA": dA_tot,
+        "dB": dB,
+        "dC": dC,
+        "dD": dD,
+        "dz": dz,
+        "ddelta_bias": ddelta_bias,
+        "dinitial_state": None if zero_state else g,
+        "out": pre_gate * (z * _sigmoid(z)) if z is not None else pre_gate,
+        "last_state": hs[L],
+    }
+
+
+# --------------------------------------------------------------------------
+# Seeded inputs with the distributions of the benchmark configurations.
+# --------------------------------------------------------------------------
+def make_inputs(batch, dim, length, dstate, *, seed=0, with_D=True, with_z=True,
+                with_bias=True, delta_softplus=True, initial_state=False,
+                valid_lengths=None, dtype=np.float32):
+    """Inputs of configs[0]/[1]: u, z ~ N(0,1); delta ~ N(0,1) with
+    delta_bias ~ U(-4,-2) and softplus; A[d, n] = -exp(log(n+1)); B, C ~ N(0,1)
+    in (B, N, L); D ~ N(0,1). One PCG64 stream per tensor."""
+    ss = np.random.SeedSequence(seed)
+    rngs = [np.random.Generator(np.random.PCG64(s)) for s in ss.spawn(10)]
+    u = rngs[0].standard_normal((batch, dim, length)).astype(dtype)
+    delta = rngs[1].standard_normal((batch, dim, length)).astype(dtype)
+    A = np.broadcast_to(-np.exp(np.log(np.arange(1, dstate + 1, dtype=np.float64))),
+                        (dim, dstate)).astype(np.float32).copy()
+    Bm = rngs[2].standard_normal((batch, dstate, length)).astype(dtype)
+    Cm = rngs[3].standard_normal((batch, dstate, length)).astype(dtype)
+    D = rngs[4].standard_normal(dim).astype(np.float32) if with_D else None
+    z = rngs[5].standard_normal((batch, dim, length)).astype(dtype) if with_z else None
+    bias = rngs[6].uniform(-4.0, -2.0, dim).astype(np.float32) if with_bias else None
+    h0 = (rngs[7].standard_normal((batch, dim, dstate)).astype(np.float32)
+          if initial_state else None)
+    dout = rngs[8].standard_normal((batch, dim, length)).astype(dtype)
+    seq_lens = None
+    if valid_lengths is not None:
+        lo, hi = valid_lengths
+        seq_lens = rngs[9].integers(lo, hi + 1, batch).astype(np.int32)
+    return {
+        "u": u, "delta": delta, "A": A, "B": Bm, "C": Cm, "D": D, "z": z,
+        "delta_bias": bias, "delta_softplus": delta_softplus,
+        "initial_state": h0, "seq_lens": seq_lens, "dout": dout,
+    }

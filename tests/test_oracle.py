@@ -1,0 +1,131 @@
+"""CPU checks that pin the oracle before the GPU tests trust it.
+
+* the reference's known-answer test: associative scan == sequential
+  recurrence (tests/test_selective_scan_cuda.py:22-52), both discretizations;
+* the fused forward in kernel layout == the reference formulation after the
+  caller-side math of S6.__call__ (mamba/mamba1.py:162-198);
+* the analytic backward == torch.autograd in float64;
+* the committed golden fixtures still match.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import selective_scan_oracle as orc
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _kat_inputs(batch=2, length=17, dim=8, n=16, seed=7):
+    rng = np.random.default_rng(seed)
+    A = -np.exp(rng.standard_normal((dim, n)))
+    deltas = np.logaddexp(rng.standard_normal((batch, length, dim)), 0.0)
+    Bs = rng.standard_normal((batch, length, n))
+    Cs = rng.standard_normal((batch, length, n))
+    u = rng.standard_normal((batch, length, dim))
+    x0 = rng.standard_normal((batch, dim, n))
+    return A, deltas, Bs, Cs, u, x0
+
+
+@pytest.mark.parametrize("use_euler", [True, False])
+def test_reference_matches_sequential_recurrence(use_euler):
+    args = _kat_inputs()
+    y, f = orc.selective_scan_reference(*args, use_euler_barB_approx=use_euler)
+    ys, fs = orc.sequential_recurrence(*args, use_euler_barB_approx=use_euler)
+    np.testing.assert_allclose(y, ys, rtol=2e-5, atol=2e-5)
+    np.testing.assert_allclose(f, fs, rtol=2e-5, atol=2e-5)
+    # float32 evaluation stays within the reference test's tolerance too
+    y32, f32 = orc.selective_scan_reference(*args, use_euler_barB_approx=use_euler,
+                                            dtype=np.float32)
+    np.testing.assert_allclose(y32, ys, rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("use_euler", [True, False])
+def test_fused_forward_matches_reference_formulation(use_euler):
+    x = orc.make_inputs(2, 8, 40, 16, seed=3, initial_state=True)
+    out, last = orc.fused_forward(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"],
+                                  x["delta_bias"], True, x["initial_state"], use_euler)
+    # caller-side math of S6.__call__/Mamba.__call__ around selective_scan
+    dl = np.logaddexp(x["delta"].astype(np.float64) + x["delta_bias"][None, :, None], 0.0)
+    y, f = orc.selective_scan_reference(
+        x["A"], dl.transpose(0, 2, 1), x["B"].transpose(0, 2, 1), x["C"].transpose(0, 2, 1),
+        x["u"].transpose(0, 2, 1), x["initial_state"], use_euler_barB_approx=use_euler)
+    y = y.transpose(0, 2, 1) + x["D"].astype(np.float64)[None, :, None] * x["u"]
+    z = x["z"].astype(np.float64)
+    y = y * z / (1.0 + np.exp(-z))
+    np.testing.assert_allclose(out, y, rtol=1e-10, atol=1e-10)
+    np.testing.assert_allclose(last, f, rtol=1e-10, atol=1e-10)
+
+
+def _torch_fused(u, delta, A, B, C, D, z, bias, h0, use_euler, mask):
+    pre = delta + bias[None, :, None]
+    dl = torch.nn.functional.softplus(pre) * mask
+    um = u * mask
+    h = h0
+    ys = []
+    for t in range(u.shape[2]):
+        dA = dl[:, :, t, None] * A[None]
+        a = torch.exp(dA)
+        bb = dl[:, :, t, None] * B[:, None, :, t] if use_euler else \
+            torch.expm1(dA) / A[None] * B[:, None, :, t]
+        h = a * h + bb * um[:, :, t, None]
+        ys.append(torch.einsum("bn,bdn->bd", C[:, :, t], h))
+    y = torch.stack(ys, 2) + D[None, :, None] * um
+    out = y * torch.nn.functional.silu(z) * mask
+    return out, h
+
+
+@pytest.mark.parametrize("use_euler", [True, False])
+@pytest.mark.parametrize("padded", [False, True])
+def test_analytic_backward_matches_autograd(use_euler, padded):
+    x = orc.make_inputs(2, 5, 23, 4, seed=13, initial_state=True,
+                        valid_lengths=(5, 23) if padded else None)
+    dlast = np.random.default_rng(1).standard_normal((2, 5, 4))
+    ref = orc.fused_backward(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"],
+                             x["delta_bias"], True, x["initial_state"], use_euler,
+                             x["seq_lens"], dout=x["dout"], dlast_state=dlast)
+    names = ["u", "delta", "A", "B", "C", "D", "z", "delta_bias", "initial_state"]
+    t = {k: torch.from_numpy(np.asarray(x[k], dtype=np.float64)).requires_grad_(True)
+         for k in names}
+    L = x["u"].shape[2]
+    if x["seq_lens"] is not None:
+        mask = torch.from_numpy((np.arange(L)[None, :] < x["seq_lens"][:, None])
+                                .astype(np.float64))[:, None, :]
+    else:
+        mask = torch.ones(1, 1, L, dtype=torch.float64)
+    out, h = _torch_fused(*(t[k] for k in names), use_euler, mask)
+    loss = (out * torch.from_numpy(x["dout"].astype(np.float64))).sum() + \
+        (h * torch.from_numpy(dlast)).sum()
+    loss.backward()
+    keys = {"u": "du", "delta": "ddelta", "A": "dA", "B": "dB", "C": "dC", "D": "dD",
+            "z": "dz", "delta_bias": "ddelta_bias", "initial_state": "dinitial_state"}
+    np.testing.assert_allclose(ref["out"] * mask.numpy(), out.detach().numpy(), rtol=1e-10,
+                               atol=1e-12)
+    for k in names:
+        np.testing.assert_allclose(ref[keys[k]], t[k].grad.numpy(), rtol=1e-9, atol=1e-11,
+                                   err_msg=k)
+
+
+def test_golden_fixtures():
+    path = GOLDEN / "fused_small.npz"
+    g = np.load(path)
+    spec = {k[5:]: g[k] for k in g.files if k.startswith("spec_")}
+    x = orc.make_inputs(int(spec["batch"]), int(spec["dim"]), int(spec["length"]),
+                        int(spec["dstate"]), seed=int(spec["seed"]), initial_state=True,
+                        valid_lengths=None)
+    np.testing.assert_equal(orc_checksum(x), g["input_checksum"])
+    ref = orc.fused_backward(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"],
+                             x["delta_bias"], True, x["initial_state"], True, None,
+                             dout=x["dout"])
+    for k in ("out", "last_state", "du", "ddelta", "dA", "dB", "dC", "dD", "dz",
+              "ddelta_bias", "dinitial_state"):
+        np.testing.assert_allclose(ref[k], g[k], rtol=1e-6, atol=1e-6, err_msg=k)
+
+
+def orc_checksum(x):
+    """float64 sums of every input tensor, to detect a changed input stream."""
+    return np.array([float(np.asarray(x[k], dtype=np.float64).sum())
+                     for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias",
+                               "initial_state", "dout")])
