@@ -241,7 +241,8 @@ def fused_backward(u, delta, A, B, C, D=None, z=None, delta_bias=None,
         "dz": dz,
         "ddelta_bias": ddelta_bias,
         "dinitial_state": None if zero_state else g,
-        "out": pre_gate * (z * _sigmoid(z)) if z is not None else pre_gate,
+        "out": (pre_gate * (z * _sigmoid(z)) if z is not None else pre_gate)
+               * (mask[:, None, :] if seq_lens is not None else 1.0),
         "last_state": hs[L],
     }
 

@@ -34,7 +34,7 @@ def test_config0_fused_fp32():
     _check(run_fused(x), oracle_fused(x))
 
 
-@pytest.mark.parametrize("length", [1, 17, 128, 255, 256, 257, 513, 2051])
+@pytest.mark.parametrize("length", [1, 17, 128, 255, 256, 257, 511, 512, 513, 1025, 2051])
 @pytest.mark.parametrize("dstate", [1, 2, 4, 8, 16])
 def test_lengths_and_states(length, dstate):
     # dim=6 leaves two idle warps in the last CTA
