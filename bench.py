@@ -115,10 +115,12 @@ def _algorithmic(cfg, esize):
     b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
     elems = b * d * L
     bnl = b * n * L
-    nch = math.ceil(L / 256)
+    nch = math.ceil(L / 512)
     cs = b * d * nch * n * 4
-    fwd = elems * 4 * esize + 2 * bnl * esize + cs          # u, delta, z in; out; B, C; carries
-    bwd = elems * 7 * esize + 4 * bnl * esize + cs          # u, delta, z, dy in; du, ddelta, dz out
+    # forward: u, delta, z in; out and the pre-gate out (kept for dz) out
+    fwd = elems * 5 * esize + 2 * bnl * esize + cs
+    # backward: u, delta, z, dy, pre-gate out in; du, ddelta, dz out
+    bwd = elems * 8 * esize + 4 * bnl * esize + cs
     # special-function-unit ops per element: N ex2 per pass, plus softplus
     # (exp, log), sigmoid(z) (exp, rcp) in the forward and softplus, sigmoid
     # of delta and sigmoid(z) in the backward
@@ -164,6 +166,7 @@ def run_gpu(args, cfg):
         u.masked_fill_(~m, 0)
 
     out = torch.empty_like(u)
+    pre = torch.empty_like(u)
     last = torch.empty(b, d, n, device=dev)
     cs = torch.empty(ssc.chunk_states_elems(b, L, d, n), device=dev)
     du, ddl, dz = torch.empty_like(u), torch.empty_like(u), torch.empty_like(u)
@@ -175,11 +178,12 @@ def run_gpu(args, cfg):
 
     def fwd():
         ssc.fused_forward_into(u, delta, A, Bm, Cm, Dp, z, bias, True, None, seq_lens,
-                               out, last, cs)
+                               out, last, cs, out_pre=pre)
 
     def bwd():
         ssc.fused_backward_into(u, delta, A, Bm, Cm, Dp, z, bias, True, None, seq_lens, cs,
-                                dout, None, du, ddl, dA, dB, dC, dDp, dz, dbias, None, ws)
+                                dout, None, du, ddl, dA, dB, dC, dDp, dz, dbias, None, ws,
+                                out_pre=pre)
 
     def step():
         fwd()

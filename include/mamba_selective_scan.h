@@ -41,7 +41,7 @@ typedef enum { MSS_F32 = 0, MSS_BF16 = 1 } mss_dtype;
 typedef enum { MSS_EULER = 0, MSS_ZOH = 1 } mss_discretization;
 
 /* Time steps covered by one saved carry (one entry of chunk_states). */
-#define MSS_CHUNK 256
+#define MSS_CHUNK 512
 
 /* Message of the last failed call on this host thread ("" if none). */
 const char* mamba_ss_last_error(void);
@@ -49,7 +49,13 @@ const char* mamba_ss_last_error(void);
 /* Library version string, e.g. "mamba-ss-b200 0.1 sm_100a". */
 const char* mamba_ss_version(void);
 
-/* Number of fp32 elements of chunk_states: batch*dim*ceil(length/256)*dstate.
+/* Returns and clears the device-side error word of the current device:
+ * bit 0 = a kernel gave up waiting (bounded) for its TMA copies and returned
+ * early, so its outputs are incomplete. Synchronous; no counterpart in the
+ * reference, whose kernels have no waits. */
+uint32_t mamba_ss_take_device_error(void);
+
+/* Number of fp32 elements of chunk_states: batch*dim*ceil(length/512)*dstate.
  * The reference sizes the same residual (batch, dim, ceil(L/2048), N, 2)
  * (mamba/selective_scan_cuda.py:129-134); it is private to the custom_vjp. */
 int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
@@ -105,7 +111,9 @@ mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
  *   h_t = exp(delta_eff*A) h_{t-1} + delta_eff*B_t*u_t          (Euler)
  *   out = (sum_n C_t h_t + D*u) * silu(z)
  * Optional pointers (D, z, delta_bias, initial_state, seq_lens, last_state,
- * dfinal_state and their gradients) may be NULL. With seq_lens, steps
+ * dfinal_state and their gradients) may be NULL. out_pre receives the
+ * pre-gate output y + D*u (io_dtype, same layout as out); the backward needs
+ * it whenever z is given, and it may be NULL when z is NULL. With seq_lens, steps
  * t >= seq_lens[b] are padding: their delta and u count as 0, their output
  * and input gradients are written as exact zeros.
  * io_dtype (MSS_F32 or MSS_BF16) types u, delta, z, B, C, out and their
@@ -117,7 +125,7 @@ mss_status mamba_ss_fused_fwd(
     const void* delta, const float* A, const void* B, const void* C,
     const float* D, const void* z, const float* delta_bias,
     int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
-    void* out, float* last_state, float* chunk_states);
+    void* out, void* out_pre, float* last_state, float* chunk_states);
 
 mss_status mamba_ss_fused_bwd(
     void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,
@@ -125,7 +133,8 @@ mss_status mamba_ss_fused_bwd(
     const void* delta, const float* A, const void* B, const void* C,
     const float* D, const void* z, const float* delta_bias,
     int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
-    const float* chunk_states, const void* dout, const float* dlast_state,
+    const float* chunk_states, const void* out_pre, const void* dout,
+    const float* dlast_state,
     void* du, void* ddelta, float* dA, void* dB, void* dC, float* dD,
     void* dz, float* ddelta_bias, float* dinitial_state, void* workspace,
     size_t workspace_bytes);

@@ -41,8 +41,8 @@ mss_status check_dims(const char* op, int io_dtype, int discretization,
   if (io_dtype != MSS_F32 && io_dtype != MSS_BF16)
     return fail(MSS_INVALID_ARGUMENT,
                 std::string(op) + ": io_dtype must be 0 (f32) or 1 (bf16)");
-  if (static_cast<int64_t>(batch) * dim > (1ll << 31) / 1 ||
-      static_cast<int64_t>(dim) * dstate > (1ll << 31))
+  if (static_cast<int64_t>(batch) * dim >= (1ll << 31) ||
+      static_cast<int64_t>(dim) * dstate >= (1ll << 31))
     return fail(MSS_INVALID_ARGUMENT, std::string(op) + ": sizes too large");
   return MSS_OK;
 }
@@ -86,6 +86,8 @@ const char* mamba_ss_last_error(void) { return g_last_error.c_str(); }
 
 const char* mamba_ss_version(void) { return "mamba-ss-b200 0.1 sm_100a"; }
 
+uint32_t mamba_ss_take_device_error(void) { return mss::take_fwd_device_error(); }
+
 int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
                                     int32_t dstate) {
   if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
@@ -104,7 +106,7 @@ mss_status mamba_ss_fused_fwd(
     const void* delta, const float* A, const void* B, const void* C,
     const float* D, const void* z, const float* delta_bias,
     int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
-    void* out, float* last_state, float* chunk_states) {
+    void* out, void* out_pre, float* last_state, float* chunk_states) {
   mss_status st = check_dims("mamba_ss_fused_fwd", io_dtype, discretization,
                              batch, length, dim, dstate);
   if (st != MSS_OK) return st;
@@ -129,6 +131,7 @@ mss_status mamba_ss_fused_fwd(
   p.h0 = initial_state;
   p.seq_lens = seq_lens;
   p.out = out;
+  p.out_pre = out_pre;
   p.last_state = last_state;
   p.chunk_states = chunk_states;
   cudaError_t e = mss::launch_fwd(p, dstate, io_dtype, discretization,
@@ -143,8 +146,8 @@ mss_status mamba_ss_fused_bwd(
     const void* delta, const float* A, const void* B, const void* C,
     const float* D, const void* z, const float* delta_bias,
     int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
-    const float* chunk_states, const void* dout, const float* dlast_state,
-    void* du, void* ddelta, float* dA, void* dB, void* dC, float* dD,
+    const float* chunk_states, const void* out_pre, const void* dout,
+    const float* dlast_state, void* du, void* ddelta, float* dA, void* dB, void* dC, float* dD,
     void* dz, float* ddelta_bias, float* dinitial_state, void* workspace,
     size_t workspace_bytes) {
   mss_status st = check_dims("mamba_ss_fused_bwd", io_dtype, discretization,
@@ -155,8 +158,9 @@ mss_status mamba_ss_fused_bwd(
     return fail(MSS_INVALID_ARGUMENT,
                 "mamba_ss_fused_bwd: u, delta, A, B, C, chunk_states, dout, du, "
                 "ddelta, dA, dB and dC must be non-null");
-  if (z && !dz)
-    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_bwd: z given without dz");
+  if (z && (!dz || !out_pre))
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_fused_bwd: z given without dz or out_pre");
   const BwdWorkspace w = bwd_layout(batch, length, dim, dstate, io_dtype);
   if (!workspace || workspace_bytes < w.total)
     return fail(MSS_INVALID_ARGUMENT,
@@ -183,6 +187,7 @@ mss_status mamba_ss_fused_bwd(
   p.h0 = initial_state;
   p.seq_lens = seq_lens;
   p.chunk_states = chunk_states;
+  p.out_pre = out_pre;
   p.dout = dout;
   p.dlast = dlast_state;
   p.du = du;
@@ -214,7 +219,7 @@ mss_status mamba_ss_fwd(void* stream, int32_t discretization, int32_t batch,
                         float* y, float* final_x, float* chunk_states) {
   return mamba_ss_fused_fwd(stream, MSS_F32, discretization, batch, length, dim,
                             dstate, u, deltas, A, B, C, nullptr, nullptr,
-                            nullptr, 0, initial_x, nullptr, y, final_x,
+                            nullptr, 0, initial_x, nullptr, y, nullptr, final_x,
                             chunk_states);
 }
 
@@ -246,8 +251,8 @@ mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
                         void* workspace, size_t workspace_bytes) {
   return mamba_ss_fused_bwd(stream, MSS_F32, discretization, batch, length, dim,
                             dstate, u, deltas, A, B, C, nullptr, nullptr,
-                            nullptr, 0, initial_x, nullptr, chunk_states, dy,
-                            dfinal_x, du, ddeltas, dA, dB, dC, nullptr, nullptr,
+                            nullptr, 0, initial_x, nullptr, chunk_states, nullptr,
+                            dy, dfinal_x, du, ddeltas, dA, dB, dC, nullptr, nullptr,
                             nullptr, dinitial_x, workspace, workspace_bytes);
 }
 

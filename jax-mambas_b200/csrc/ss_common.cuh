@@ -20,7 +20,7 @@
 
 namespace mss {
 
-constexpr int kItems = 8;                   // steps per lane per chunk
+constexpr int kItems = 16;                  // steps per lane per chunk
 constexpr int kChunk = 32 * kItems;         // steps per chunk (== MSS_CHUNK)
 static_assert(kChunk == MSS_CHUNK, "chunk size must match the public header");
 constexpr float kLog2e = 1.4426950408889634f;
@@ -28,6 +28,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 struct FwdParams {
   int batch, dim, seqlen, n_chunks;
   int delta_softplus;
+  int tma_ok;  // rows may be staged with TMA bulk copies (set by the launcher)
   const void* u;
   const void* delta;
   const void* z;
@@ -39,6 +40,7 @@ struct FwdParams {
   const float* h0;
   const int32_t* seq_lens;
   void* out;
+  void* out_pre;  // optional: y + D*u before the gate (read by the backward for dz)
   float* last_state;
   float* chunk_states;
 };
@@ -57,6 +59,7 @@ struct BwdParams {
   const float* h0;
   const int32_t* seq_lens;
   const float* chunk_states;
+  const void* out_pre;  // y + D*u saved by the forward (needed when z is given)
   const void* dout;
   const float* dlast;
   void* du;
@@ -89,6 +92,9 @@ struct Elem<__nv_bfloat16> {
     *p = __float2bfloat16_rn(v);
   }
 };
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
 
 // Loads kItems consecutive elements row[t .. t+kItems) as fp32; elements at or
 // beyond `limit` read as 0. Uses 16-byte loads when the run is whole and
@@ -181,6 +187,85 @@ __device__ __forceinline__ float sigmoid(float x) {
   return 1.f / (1.f + expf(-x));
 }
 
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)), jax.nn.softplus's function
+// (mamba/mamba1.py:76,165), evaluated without overflow for any x.
+__device__ __forceinline__ float softplus_f(float x) {
+  return fmaxf(x, 0.f) + log1pf(__expf(-fabsf(x)));
+}
+
+// 1 / (1 + e^-x) from one SFU exponential and one SFU reciprocal.
+__device__ __forceinline__ float sigmoid_f(float x) {
+  return __fdividef(1.f, 1.f + __expf(-x));
+}
+
+__device__ __forceinline__ float silu_f(float z) { return z * sigmoid_f(z); }
+
+// ------------------------------------------------- TMA bulk copies, mbarriers
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the TMA (async proxy).
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (TMA) writes to the same buffers.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// 1-D TMA copy global -> shared of `bytes` (multiple of 16, both addresses
+// 16-byte aligned); completion is counted on `bar`.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete, giving up after a bounded
+// number of polls (each try_wait suspends the thread for a short,
+// hardware-defined time). Returns false on timeout.
+constexpr uint32_t kWaitPolls = 1u << 22;
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// Bit set in a kernel's device error word when it gave up waiting for its
+// TMA copies (see mamba_ss_take_device_error()).
+constexpr unsigned int kErrTmaTimeout = 1u;
+
 // ------------------------------------------------------------ warp scans
 // Inclusive scan over lanes of the affine maps h -> P h + H, composed left
 // to right: lane i ends with the composition of lanes 0..i.
@@ -208,6 +293,27 @@ __device__ __forceinline__ void warp_scan_rev(float& P, float& G, int lane) {
       P *= Pn;
     }
   }
+}
+
+// ------------------------------------------------------- packed fp32 pairs
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  return __ffma2_rn(a, b, c);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
+
+// Loads a run as kItems/2 pairs (items 2i, 2i+1).
+template <typename T>
+__device__ __forceinline__ void load_run2(const T* row, int t, int limit,
+                                          float2 (&v)[kItems / 2]) {
+  load_run(row, t, limit, reinterpret_cast<float(&)[kItems]>(v));
+}
+
+template <typename T>
+__device__ __forceinline__ void store_run2(T* row, int t, int limit,
+                                           const float2 (&v)[kItems / 2]) {
+  store_run(row, t, limit, reinterpret_cast<const float(&)[kItems]>(v));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

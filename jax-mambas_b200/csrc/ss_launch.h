@@ -18,4 +18,7 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream);
 
+// Returns and clears the forward kernel's device error word (0 = no error).
+unsigned int take_fwd_device_error();
+
 }  // namespace mss

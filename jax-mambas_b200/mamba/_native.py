@@ -22,7 +22,7 @@ MSS_F32 = 0
 MSS_BF16 = 1
 MSS_EULER = 0
 MSS_ZOH = 1
-CHUNK = 256
+CHUNK = 512
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -32,6 +32,7 @@ _f32p = ctypes.c_void_p  # device pointers are passed as integers
 SIGNATURES = {
     "mamba_ss_last_error": (ctypes.c_char_p, []),
     "mamba_ss_version": (ctypes.c_char_p, []),
+    "mamba_ss_take_device_error": (ctypes.c_uint32, []),
     "mamba_ss_chunk_states_elems": (ctypes.c_int64, [_i32, _i32, _i32, _i32]),
     "mamba_ss_bwd_workspace_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     "mamba_ss_fwd": (ctypes.c_int, [_c_void_p, _i32, _i32, _i32, _i32, _i32] + [_f32p] * 9),
@@ -45,14 +46,14 @@ SIGNATURES = {
         [_c_void_p, _i32, _i32, _i32, _i32, _i32, _i32]
         + [_c_void_p] * 8  # u delta A B C D z delta_bias
         + [_i32]  # delta_softplus
-        + [_c_void_p] * 5,  # initial_state seq_lens out last_state chunk_states
+        + [_c_void_p] * 6,  # initial_state seq_lens out out_pre last_state chunk_states
     ),
     "mamba_ss_fused_bwd": (
         ctypes.c_int,
         [_c_void_p, _i32, _i32, _i32, _i32, _i32, _i32]
         + [_c_void_p] * 8  # u delta A B C D z delta_bias
         + [_i32]  # delta_softplus
-        + [_c_void_p] * 15  # initial_state seq_lens chunk_states dout dlast du ddelta dA dB dC dD dz dbias dinit workspace
+        + [_c_void_p] * 16  # initial_state seq_lens chunk_states out_pre dout dlast du ddelta dA dB dC dD dz dbias dinit workspace
         + [ctypes.c_size_t],
     ),
 }

@@ -153,7 +153,7 @@ def _io_dtype(t):
 
 def fused_forward_into(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
                        initial_state, seq_lens, out, last_state, chunk_states,
-                       zoh=False):
+                       zoh=False, out_pre=None):
     """Launch the fused forward on the current stream into given buffers."""
     lib = _lib()
     batch, dim, length = u.shape
@@ -162,14 +162,14 @@ def fused_forward_into(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
         _stream(u.device), _io_dtype(u), int(zoh), batch, length, dim, dstate,
         _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z),
         _ptr(delta_bias), int(bool(delta_softplus)), _ptr(initial_state),
-        _ptr(seq_lens), _ptr(out), _ptr(last_state), _ptr(chunk_states))
+        _ptr(seq_lens), _ptr(out), _ptr(out_pre), _ptr(last_state), _ptr(chunk_states))
     _native.check(lib, st)
 
 
 def fused_backward_into(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
                         initial_state, seq_lens, chunk_states, dout, dlast_state,
                         du, ddelta, dA, dB, dC, dD, dz, ddelta_bias,
-                        dinitial_state, workspace, zoh=False):
+                        dinitial_state, workspace, zoh=False, out_pre=None):
     """Launch the fused backward on the current stream into given buffers."""
     lib = _lib()
     batch, dim, length = u.shape
@@ -178,7 +178,7 @@ def fused_backward_into(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
         _stream(u.device), _io_dtype(u), int(zoh), batch, length, dim, dstate,
         _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z),
         _ptr(delta_bias), int(bool(delta_softplus)), _ptr(initial_state),
-        _ptr(seq_lens), _ptr(chunk_states), _ptr(dout), _ptr(dlast_state),
+        _ptr(seq_lens), _ptr(chunk_states), _ptr(out_pre), _ptr(dout), _ptr(dlast_state),
         _ptr(du), _ptr(ddelta), _ptr(dA), _ptr(dB), _ptr(dC), _ptr(dD),
         _ptr(dz), _ptr(ddelta_bias), _ptr(dinitial_state), _ptr(workspace),
         0 if workspace is None else workspace.numel())
@@ -245,20 +245,21 @@ class _FusedScan(torch.autograd.Function):
         batch, dim, length = u.shape
         n = A.shape[1]
         out = torch.empty_like(u)
+        pre = torch.empty_like(u) if z is not None else None
         last = torch.empty((batch, dim, n), dtype=torch.float32, device=u.device)
         cs = torch.empty(chunk_states_elems(batch, length, dim, n),
                          dtype=torch.float32, device=u.device)
         fused_forward_into(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
-                           initial_state, seq_lens, out, last, cs, zoh)
+                           initial_state, seq_lens, out, last, cs, zoh, pre)
         ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, initial_state,
-                              seq_lens, cs)
+                              seq_lens, cs, pre)
         ctx.delta_softplus = delta_softplus
         ctx.zoh = zoh
         return out, last
 
     @staticmethod
     def backward(ctx, dout, dlast):
-        u, delta, A, B, C, D, z, delta_bias, h0, seq_lens, cs = ctx.saved_tensors
+        u, delta, A, B, C, D, z, delta_bias, h0, seq_lens, cs, pre = ctx.saved_tensors
         batch, dim, length = u.shape
         n = A.shape[1]
         if dout is None:
@@ -277,7 +278,7 @@ class _FusedScan(torch.autograd.Function):
         ws = _alloc_workspace(batch, length, dim, n, _io_dtype(u), u.device)
         fused_backward_into(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus,
                             h0, seq_lens, cs, dout, dlast, du, ddelta, dA, dB, dC,
-                            dD, dz, dbias, dh0, ws, ctx.zoh)
+                            dD, dz, dbias, dh0, ws, ctx.zoh, pre)
         return du, ddelta, dA, dB, dC, dD, dz, dbias, dh0, None, None, None
 
 

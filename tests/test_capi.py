@@ -39,8 +39,8 @@ def test_bindings_cover_the_header():
 
 
 def test_sizes(lib):
-    assert lib.mamba_ss_chunk_states_elems(2, 256, 128, 16) == 2 * 128 * 1 * 16
-    assert lib.mamba_ss_chunk_states_elems(2, 257, 128, 16) == 2 * 128 * 2 * 16
+    assert lib.mamba_ss_chunk_states_elems(2, 512, 128, 16) == 2 * 128 * 1 * 16
+    assert lib.mamba_ss_chunk_states_elems(2, 513, 128, 16) == 2 * 128 * 2 * 16
     assert lib.mamba_ss_chunk_states_elems(0, 257, 128, 16) == 0
     f32 = lib.mamba_ss_bwd_workspace_bytes(8, 2048, 1536, 16, 0)
     bf16 = lib.mamba_ss_bwd_workspace_bytes(8, 2048, 1536, 16, 1)
@@ -62,14 +62,14 @@ def test_invalid_arguments(lib, case, msg):
     p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
     st = lib.mamba_ss_fused_fwd(None, a["io"], a["disc"], a["batch"], a["length"], a["dim"],
                                 a["dstate"], p, p, p, p, p, None, None, None, 0, None, None,
-                                p, None, p)
+                                p, None, None, p)
     assert st == 1
     assert msg in lib.mamba_ss_last_error()
 
 
 def test_null_required_pointer(lib):
     st = lib.mamba_ss_fused_fwd(None, 0, 0, 1, 8, 4, 16, None, None, None, None, None, None,
-                                None, None, 0, None, None, None, None, None)
+                                None, None, 0, None, None, None, None, None, None)
     assert st == 1
     assert b"non-null" in lib.mamba_ss_last_error()
 
@@ -77,8 +77,8 @@ def test_null_required_pointer(lib):
 def test_backward_rejects_small_workspace(lib):
     p = ctypes.c_void_p(256)
     st = lib.mamba_ss_fused_bwd(None, 0, 0, 1, 8, 4, 16, p, p, p, p, p, None, None, None, 0,
-                                None, None, p, p, None, p, p, p, p, p, None, None, None, None,
-                                p, 16)
+                                None, None, p, None, p, None, p, p, p, p, p, None, None, None,
+                                None, p, 16)
     assert st == 1
     assert b"workspace needs" in lib.mamba_ss_last_error()
 

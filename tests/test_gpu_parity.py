@@ -121,6 +121,9 @@ def test_determinism():
         np.testing.assert_array_equal(r1[k], r2[k], err_msg=k)
     for k in ("dB", "dC"):  # channel sums use float atomics across CTAs
         assert_close(r1[k], r2[k], 1e-5, k)
+    from mamba import _native
+
+    assert _native.load().mamba_ss_take_device_error() == 0
 
 
 def test_poisoned_outputs_are_overwritten():
@@ -134,8 +137,10 @@ def test_poisoned_outputs_are_overwritten():
     out = torch.full_like(t["u"], float("nan"))
     last = torch.full((b, d, 16), float("nan"), device=dev)
     cs = torch.full((ssc.chunk_states_elems(b, L, d, 16),), float("nan"), device=dev)
+    pre = torch.full_like(t["u"], float("nan"))
     ssc.fused_forward_into(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
-                           t["delta_bias"], True, t["initial_state"], None, out, last, cs)
+                           t["delta_bias"], True, t["initial_state"], None, out, last, cs,
+                           out_pre=pre)
     grads = [torch.full_like(t[k], float("nan")) for k in
              ("u", "delta", "A", "B", "C", "D", "z", "delta_bias", "initial_state")]
     ws = ssc._alloc_workspace(b, L, d, 16, 0, dev)
@@ -143,9 +148,9 @@ def test_poisoned_outputs_are_overwritten():
     du, dd, dA, dB, dC, dD, dz, dbias, dh0 = grads
     ssc.fused_backward_into(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
                             t["delta_bias"], True, t["initial_state"], None, cs, t["dout"],
-                            None, du, dd, dA, dB, dC, dD, dz, dbias, dh0, ws)
+                            None, du, dd, dA, dB, dC, dD, dz, dbias, dh0, ws, out_pre=pre)
     torch.cuda.synchronize()
-    for v in [out, last, cs] + grads:
+    for v in [out, last, cs, pre] + grads:
         assert torch.isfinite(v).all()
 
 
