@@ -8,11 +8,14 @@
 // Decomposition: the recurrence runs sequentially in time inside each lane,
 // with no cross-lane scan. A lane owns kS states of one channel; kLPC = NS/kS
 // lanes cover a channel, so a warp holds 32/kLPC channels and a CTA holds
-// kCh = 32 channels of one batch. The CTA walks L in tiles of kTile steps,
-// double-buffered:
-//   0. TMA: one thread issues 1-D bulk copies of the tile's rows of delta, u,
-//      z (per channel) and B, C (per state) into a staging buffer, completing
-//      on an mbarrier; the next tile's copies fly while this tile computes;
+// kCh channels of one batch (one warp for N = 16, so that every CTA of a
+// Mamba-size layer is resident at once). The CTA walks L in tiles of kTile
+// steps, double-buffered:
+//   0. TMA: one thread issues five 2-D tensor copies per tile (delta, u, z as
+//      [kCh channels x kTile steps], B, C as [N states x kTile steps]) into a
+//      staging buffer, completing on an mbarrier; the TMA zero-fills past the
+//      sequence end and past the last channel; the next tile's copies fly
+//      while this tile computes;
 //   1. transform: delta_eff = softplus(delta + bias), delta_eff*u and D*u are
 //      formed once per element into fp32 work tiles, B and C are widened;
 //   2. scan: each lane steps through the tile; per step and state one
@@ -23,6 +26,10 @@
 // The state at every MSS_CHUNK boundary is saved for the backward. Rows whose
 // length or base address is not 16-byte aligned take the same path with the
 // staging done by plain loads instead of TMA.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
 #include "ss_common.cuh"
 #include "ss_launch.h"
 
@@ -30,8 +37,7 @@ namespace mss {
 
 __device__ unsigned int g_fwd_device_error = 0;
 
-constexpr int kCh = 32;    // channels per CTA
-constexpr int kTile = 64;  // steps staged per pass
+constexpr int kTile = 32;  // steps staged per pass
 constexpr int kPad = 4;    // row padding (floats) of the fp32 work tiles
 constexpr int kRow = kTile + kPad;
 static_assert(kChunk % kTile == 0, "a carry checkpoint must end a tile");
@@ -41,35 +47,73 @@ struct FwdCfg {
   static constexpr int kS = NS < 4 ? NS : 4;  // states per lane
   static constexpr int kLPC = NS / kS;        // lanes per channel
   static constexpr int kCPW = 32 / kLPC;      // channels per warp
+  static constexpr int kCh = kCPW < 8 ? 8 : kCPW;  // channels per CTA
   static constexpr int kWarps = kCh / kCPW;   // warps per CTA
   static constexpr int kThreads = kWarps * 32;
 };
 
+// Tensor maps of the five TMA-staged inputs (see launch_fwd).
+struct FwdMaps {
+  CUtensorMap d, u, z, b, c;
+};
+
 template <int NS, typename T>
 struct FwdShared {
-  // staging, written by TMA (two buffers)
-  T rawD[2][kCh][kTile];
+  static constexpr int kCh = FwdCfg<NS>::kCh;
+  // staging, written by TMA (two buffers); every block is a multiple of 128 B
+  alignas(128) T rawD[2][kCh][kTile];
   T rawU[2][kCh][kTile];
   T rawZ[2][kCh][kTile];
-  T rawB[2][NS][kTile];
-  T rawC[2][NS][kTile];
+  // B/C blocks padded to whole 1024-byte units: fp32 B/C are staged with the
+  // TMA's 128-byte swizzle, whose pattern repeats every 8 rows of 128 bytes.
+  static constexpr int kNSP =
+      (NS * kTile * sizeof(T) + 1023) / 1024 * 1024 / (kTile * sizeof(T));
+  alignas(1024) T rawB[2][kNSP][kTile];
+  alignas(1024) T rawC[2][kNSP][kTile];
   // fp32 work tiles
   float dlt[kCh][kRow];  // delta_eff
   float dlu[kCh][kRow];  // delta_eff * u   (ZOH: u)
   float ys[kCh][kRow];   // D u, then + sum_n C_t h_t
-  float Bs[NS][kRow];
-  float Cs[NS][kRow];
+  // widened B/C (bf16 I/O only; fp32 I/O reads the swizzled staging)
+  float Bs[sizeof(T) == 4 ? 1 : NS][kRow];
+  float Cs[sizeof(T) == 4 ? 1 : NS][kRow];
   uint64_t bar[2];
 };
 
+// Four consecutive staged elements as fp32 (16-byte or 8-byte aligned).
+__device__ __forceinline__ void load4_smem(const float* src, float (&v)[4]) {
+  const float4 f = *reinterpret_cast<const float4*>(src);
+  v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+}
+__device__ __forceinline__ void load4_smem(const __nv_bfloat16* src, float (&v)[4]) {
+  const uint2 w = *reinterpret_cast<const uint2*>(src);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void store4_global(float* dst, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4_global(__nv_bfloat16* dst, const float (&v)[4]) {
+  uint2 w;
+  *reinterpret_cast<__nv_bfloat162*>(&w.x) = __floats2bfloat162_rn(v[0], v[1]);
+  *reinterpret_cast<__nv_bfloat162*>(&w.y) = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(dst) = w;
+}
+
 template <int NS, typename T, bool kZOH>
 __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
-    ss_fwd_kernel(const FwdParams p) {
+    ss_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   using Cfg = FwdCfg<NS>;
   constexpr int kS = Cfg::kS;
   constexpr int kLPC = Cfg::kLPC;
+  constexpr int kCh = Cfg::kCh;
   constexpr int kThreads = Cfg::kThreads;
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  // fp32 B/C are read straight from the (swizzled) TMA staging; B/C rows past
+  // the sequence end are zero-filled by the TMA, and their steps carry
+  // delta = 0, so they never touch the state.
+  constexpr bool kDirectBC = sizeof(T) == 4;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   FwdShared<NS, T>& sh = *reinterpret_cast<FwdShared<NS, T>*>(smem_raw);
 
   const int tid = threadIdx.x;
@@ -109,7 +153,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
   const T* C_b = static_cast<const T*>(p.C) + static_cast<size_t>(b) * NS * L;
   const bool use_tma = p.tma_ok != 0;
 
-  // Issues the TMA copies of tile `k` into staging buffer k % 2.
+  // Issues the TMA copies of tile `k` into staging buffer k % 2 (one thread).
   auto issue = [&](int k) {
     const int s = k & 1;
     const int t0 = k * kTile;
@@ -118,20 +162,15 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       mbar_arrive_expect_tx(bar, 0);
       return;
     }
-    const uint32_t bytes = static_cast<uint32_t>(min(kTile, L - t0) * sizeof(T));
-    const uint32_t rows = 2 * n_ch + (z_b ? n_ch : 0) + 2 * NS;
-    mbar_arrive_expect_tx(bar, rows * bytes);
-    for (int c = 0; c < n_ch; ++c) {
-      const size_t off = static_cast<size_t>(d0 + c) * L + t0;
-      tma_load_1d(&sh.rawD[s][c][0], dl_b + off, bytes, bar);
-      tma_load_1d(&sh.rawU[s][c][0], u_b + off, bytes, bar);
-      if (z_b) tma_load_1d(&sh.rawZ[s][c][0], z_b + off, bytes, bar);
-    }
-    for (int n = 0; n < NS; ++n) {
-      const size_t off = static_cast<size_t>(n) * L + t0;
-      tma_load_1d(&sh.rawB[s][n][0], B_b + off, bytes, bar);
-      tma_load_1d(&sh.rawC[s][n][0], C_b + off, bytes, bar);
-    }
+    constexpr uint32_t kChBytes = kCh * kTile * sizeof(T);
+    constexpr uint32_t kNBytes = NS * kTile * sizeof(T);
+    mbar_arrive_expect_tx(bar, (z_b ? 3 : 2) * kChBytes + 2 * kNBytes);
+    const int rc = b * p.dim + d0;  // first channel row
+    tma_load_2d(&sh.rawD[s][0][0], &maps.d, t0, rc, bar);
+    tma_load_2d(&sh.rawU[s][0][0], &maps.u, t0, rc, bar);
+    if (z_b) tma_load_2d(&sh.rawZ[s][0][0], &maps.z, t0, rc, bar);
+    tma_load_2d(&sh.rawB[s][0][0], &maps.b, t0, b * NS, bar);
+    tma_load_2d(&sh.rawC[s][0][0], &maps.c, t0, b * NS, bar);
   };
 
   const int n_tiles = (L + kTile - 1) / kTile;
@@ -140,9 +179,9 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       mbar_init(&sh.bar[0], 1);
       mbar_init(&sh.bar[1], 1);
       fence_mbar_init();
-      issue(0);
     }
     __syncthreads();
+    if (tid == 0) issue(0);
   }
 
   for (int k = 0; k < n_tiles; ++k) {
@@ -166,45 +205,70 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
     }
 
     if (t0 < len) {
-      // ---- 1. transform the tile into fp32 work tiles
-      for (int i = tid; i < kCh * kTile; i += kThreads) {
-        const int c = i / kTile, tt = i % kTile;
-        const int t = t0 + tt;
-        float dv = 0.f, du = 0.f, yd = 0.f;
-        if (c < n_ch && t < len) {
-          float x, uv;
+      // ---- 1. transform the tile into fp32 work tiles, 4 steps per item
+      for (int i = tid; i < kCh * (kTile / 4); i += kThreads) {
+        const int c = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
+        float x[4] = {0.f, 0.f, 0.f, 0.f}, uv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (c < n_ch) {
           if (use_tma) {
-            x = to_f32(sh.rawD[s][c][tt]);
-            uv = to_f32(sh.rawU[s][c][tt]);
+            load4_smem(&sh.rawD[s][c][tt], x);
+            load4_smem(&sh.rawU[s][c][tt], uv);
           } else {
-            const size_t off = static_cast<size_t>(d0 + c) * L + t;
-            x = Elem<T>::ld(dl_b + off);
-            uv = Elem<T>::ld(u_b + off);
+            const size_t off = static_cast<size_t>(d0 + c) * L + t0 + tt;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (t0 + tt + e < len) {
+                x[e] = Elem<T>::ld(dl_b + off + e);
+                uv[e] = Elem<T>::ld(u_b + off + e);
+              }
+            }
           }
-          if (p.delta_bias) x += __ldg(p.delta_bias + d0 + c);
-          dv = p.delta_softplus ? softplus_f(x) : x;
-          du = kZOH ? uv : dv * uv;
-          if (p.D) yd = __ldg(p.D + d0 + c) * uv;
         }
-        sh.dlt[c][tt] = dv;
-        sh.dlu[c][tt] = du;
-        sh.ys[c][tt] = yd;
+        const float bias = (p.delta_bias && c < n_ch) ? __ldg(p.delta_bias + d0 + c) : 0.f;
+        const float Dd = (p.D && c < n_ch) ? __ldg(p.D + d0 + c) : 0.f;
+        float dv[4], du[4], yd[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool valid = c < n_ch && t0 + tt + e < len;
+          const float xe = x[e] + bias;
+          const float de = p.delta_softplus ? softplus_f(xe) : xe;
+          dv[e] = valid ? de : 0.f;
+          du[e] = valid ? (kZOH ? uv[e] : de * uv[e]) : 0.f;
+          yd[e] = valid ? Dd * uv[e] : 0.f;
+        }
+        *reinterpret_cast<float4*>(&sh.dlt[c][tt]) = make_float4(dv[0], dv[1], dv[2], dv[3]);
+        *reinterpret_cast<float4*>(&sh.dlu[c][tt]) = make_float4(du[0], du[1], du[2], du[3]);
+        *reinterpret_cast<float4*>(&sh.ys[c][tt]) = make_float4(yd[0], yd[1], yd[2], yd[3]);
       }
-      for (int i = tid; i < NS * kTile; i += kThreads) {
-        const int n = i / kTile, tt = i % kTile;
-        const int t = t0 + tt;
-        float bv = 0.f, cv = 0.f;
-        if (t < len) {
+      if (!(kDirectBC && use_tma)) {
+        for (int i = tid; i < NS * (kTile / 4); i += kThreads) {
+          const int n = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
+          float bv[4] = {0.f, 0.f, 0.f, 0.f}, cv[4] = {0.f, 0.f, 0.f, 0.f};
           if (use_tma) {
-            bv = to_f32(sh.rawB[s][n][tt]);
-            cv = to_f32(sh.rawC[s][n][tt]);
+            load4_smem(&sh.rawB[s][n][tt], bv);
+            load4_smem(&sh.rawC[s][n][tt], cv);
           } else {
-            bv = Elem<T>::ld(B_b + static_cast<size_t>(n) * L + t);
-            cv = Elem<T>::ld(C_b + static_cast<size_t>(n) * L + t);
+            const size_t off = static_cast<size_t>(n) * L + t0 + tt;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (t0 + tt + e < len) {
+                bv[e] = Elem<T>::ld(B_b + off + e);
+                cv[e] = Elem<T>::ld(C_b + off + e);
+              }
+            }
+          }
+          const float4 b4 = make_float4(bv[0], bv[1], bv[2], bv[3]);
+          const float4 c4 = make_float4(cv[0], cv[1], cv[2], cv[3]);
+          if constexpr (kDirectBC) {
+            // fp32 without TMA: write the layout the TMA swizzle would produce
+            const int col = ((tt >> 2) ^ (n & 7)) << 2;
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(&sh.rawB[s][n][0]) + col) = b4;
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(&sh.rawC[s][n][0]) + col) = c4;
+          } else {
+            *reinterpret_cast<float4*>(&sh.Bs[n][tt]) = b4;
+            *reinterpret_cast<float4*>(&sh.Cs[n][tt]) = c4;
           }
         }
-        sh.Bs[n][tt] = bv;
-        sh.Cs[n][tt] = cv;
       }
       __syncthreads();
 
@@ -222,8 +286,18 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
           const int n = q + kLPC * j;
-          const float4 B4 = *reinterpret_cast<const float4*>(&sh.Bs[n][tt]);
-          const float4 C4 = *reinterpret_cast<const float4*>(&sh.Cs[n][tt]);
+          float4 B4, C4;
+          if constexpr (kDirectBC) {
+            // 16-byte chunk tt/4 of row n sits at chunk (tt/4) ^ (n & 7)
+            const int col = ((tt >> 2) ^ (n & 7)) << 2;
+            B4 = *reinterpret_cast<const float4*>(
+                reinterpret_cast<const float*>(&sh.rawB[s][n][0]) + col);
+            C4 = *reinterpret_cast<const float4*>(
+                reinterpret_cast<const float*>(&sh.rawC[s][n][0]) + col);
+          } else {
+            B4 = *reinterpret_cast<const float4*>(&sh.Bs[n][tt]);
+            C4 = *reinterpret_cast<const float4*>(&sh.Cs[n][tt]);
+          }
           const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
           const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
           const float2 a2p = dup2(a2[j]);
@@ -285,24 +359,43 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
     }
     __syncthreads();
 
-    // ---- 3. emit out = (y + D u) * silu(z), and y + D u
-    for (int i = tid; i < kCh * kTile; i += kThreads) {
-      const int c = i / kTile, tt = i % kTile;
+    // ---- 3. emit out = (y + D u) * silu(z), and y + D u, 4 steps per item
+    for (int i = tid; i < kCh * (kTile / 4); i += kThreads) {
+      const int c = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
       const int t = t0 + tt;
       if (c >= n_ch || t >= L) continue;
       const size_t off = static_cast<size_t>(d0 + c) * L + t;
-      float o = 0.f, pre = 0.f;
+      float o[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f};
       if (t < len) {
-        pre = sh.ys[c][tt];
+        float zv[4];
         if (z_b) {
-          const float zv = use_tma ? to_f32(sh.rawZ[s][c][tt]) : Elem<T>::ld(z_b + off);
-          o = pre * silu_f(zv);
-        } else {
-          o = pre;
+          if (use_tma) {
+            load4_smem(&sh.rawZ[s][c][tt], zv);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (t + e < len) {
+            pre[e] = sh.ys[c][tt + e];
+            o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
+          }
         }
       }
-      Elem<T>::st(out_b + off, o);
-      if (pre_b) Elem<T>::st(pre_b + off, pre);
+      if (use_tma) {  // whole, aligned groups: L is a multiple of 4 here
+        store4_global(out_b + off, o);
+        if (pre_b) store4_global(pre_b + off, pre);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (t + e < L) {
+            Elem<T>::st(out_b + off + e, o[e]);
+            if (pre_b) Elem<T>::st(pre_b + off + e, pre[e]);
+          }
+        }
+      }
     }
     __syncthreads();
   }
@@ -314,29 +407,71 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
 }
 
 template <int NS, typename T, bool kZOH>
-static cudaError_t launch_fwd_t(const FwdParams& p, cudaStream_t stream) {
+static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps,
+                                cudaStream_t stream) {
   using Cfg = FwdCfg<NS>;
   const size_t smem = sizeof(FwdShared<NS, T>);
   auto kern = ss_fwd_kernel<NS, T, kZOH>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  dim3 grid((p.dim + kCh - 1) / kCh, p.batch);
-  kern<<<grid, Cfg::kThreads, smem, stream>>>(p);
+  dim3 grid((p.dim + Cfg::kCh - 1) / Cfg::kCh, p.batch);
+  kern<<<grid, Cfg::kThreads, smem, stream>>>(p, maps);
   return cudaPeekAtLastError();
 }
 
 template <typename T, bool kZOH>
-static cudaError_t launch_fwd_n(const FwdParams& p, int dstate,
+static cudaError_t launch_fwd_n(const FwdParams& p, const FwdMaps& maps, int dstate,
                                 cudaStream_t stream) {
   switch (dstate) {
-    case 1: return launch_fwd_t<1, T, kZOH>(p, stream);
-    case 2: return launch_fwd_t<2, T, kZOH>(p, stream);
-    case 4: return launch_fwd_t<4, T, kZOH>(p, stream);
-    case 8: return launch_fwd_t<8, T, kZOH>(p, stream);
-    case 16: return launch_fwd_t<16, T, kZOH>(p, stream);
+    case 1: return launch_fwd_t<1, T, kZOH>(p, maps, stream);
+    case 2: return launch_fwd_t<2, T, kZOH>(p, maps, stream);
+    case 4: return launch_fwd_t<4, T, kZOH>(p, maps, stream);
+    case 8: return launch_fwd_t<8, T, kZOH>(p, maps, stream);
+    case 16: return launch_fwd_t<16, T, kZOH>(p, maps, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+static int fwd_channels_per_cta(int dstate) {
+  switch (dstate) {
+    case 1: return FwdCfg<1>::kCh;
+    case 2: return FwdCfg<2>::kCh;
+    case 4: return FwdCfg<4>::kCh;
+    case 8: return FwdCfg<8>::kCh;
+    default: return FwdCfg<16>::kCh;
+  }
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// Row-major [rows][L] tensor, boxes of [box_rows][kTile]; zero fill outside.
+static bool encode_rows(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
+                        uint64_t L, uint32_t box_rows, bool swizzle128 = false) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
+  const cuuint64_t dims[2] = {L, rows};
+  const cuuint64_t strides[1] = {L * esize};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTile), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, io_dtype == MSS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+            2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static bool aligned16(const void* ptr) {
@@ -347,16 +482,28 @@ cudaError_t launch_fwd(const FwdParams& p_in, int dstate, int io_dtype, int zoh,
                        cudaStream_t stream) {
   FwdParams p = p_in;
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
-  // TMA rows need 16-byte aligned starts and sizes: whole rows of L elements
-  // and tiles of kTile elements must both be multiples of 16 bytes.
+  // TMA needs 16-byte aligned bases and row strides (L * esize).
   p.tma_ok = (p.seqlen * esize) % 16 == 0 && aligned16(p.u) && aligned16(p.delta) &&
              aligned16(p.B) && aligned16(p.C) && (!p.z || aligned16(p.z));
-  if (io_dtype == MSS_BF16) {
-    return zoh ? launch_fwd_n<__nv_bfloat16, true>(p, dstate, stream)
-               : launch_fwd_n<__nv_bfloat16, false>(p, dstate, stream);
+  FwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (p.tma_ok) {
+    const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
+    const uint64_t brows = static_cast<uint64_t>(p.batch) * dstate;
+    const uint32_t ch = static_cast<uint32_t>(fwd_channels_per_cta(dstate));
+    const uint64_t L = p.seqlen;
+    p.tma_ok = encode_rows(&maps.d, p.delta, io_dtype, rows, L, ch) &&
+               encode_rows(&maps.u, p.u, io_dtype, rows, L, ch) &&
+               (!p.z || encode_rows(&maps.z, p.z, io_dtype, rows, L, ch)) &&
+               encode_rows(&maps.b, p.B, io_dtype, brows, L, dstate, io_dtype == MSS_F32) &&
+               encode_rows(&maps.c, p.C, io_dtype, brows, L, dstate, io_dtype == MSS_F32);
   }
-  return zoh ? launch_fwd_n<float, true>(p, dstate, stream)
-             : launch_fwd_n<float, false>(p, dstate, stream);
+  if (io_dtype == MSS_BF16) {
+    return zoh ? launch_fwd_n<__nv_bfloat16, true>(p, maps, dstate, stream)
+               : launch_fwd_n<__nv_bfloat16, false>(p, maps, dstate, stream);
+  }
+  return zoh ? launch_fwd_n<float, true>(p, maps, dstate, stream)
+             : launch_fwd_n<float, false>(p, maps, dstate, stream);
 }
 
 unsigned int take_fwd_device_error() {
