@@ -139,6 +139,34 @@ mss_status mamba_ss_fused_bwd(
     void* dz, float* ddelta_bias, float* dinitial_state, void* workspace,
     size_t workspace_bytes);
 
+/* ---------------------------------------------------------------------------
+ * Allocation-free backward. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory (a host runtime that owns
+ * all device memory and only passes tensor pointers across its FFI, or code
+ * running where cudaMalloc is not allowed): same arguments and results as
+ * mamba_ss_fused_bwd minus the workspace, which comes instead from a fixed
+ * 16 MiB array inside the library (mamba_ss_noalloc_scratch_bytes()), held on
+ * every GPU that loads the library until the process exits. Problems needing
+ * more scratch than that (mamba_ss_bwd_workspace_bytes) are rejected with
+ * MSS_INVALID_ARGUMENT. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture. All calls on a device share the
+ * array, so calls whose GPU work overlaps (unordered streams) race and give
+ * wrong results. Nothing is allocated or freed.
+ * ------------------------------------------------------------------------- */
+size_t mamba_ss_noalloc_scratch_bytes(void);
+
+mss_status mamba_ss_fused_bwd_noalloc(
+    void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,
+    int32_t length, int32_t dim, int32_t dstate, const void* u,
+    const void* delta, const float* A, const void* B, const void* C,
+    const float* D, const void* z, const float* delta_bias,
+    int32_t delta_softplus, const float* initial_state, const int32_t* seq_lens,
+    const float* chunk_states, const void* out_pre, const void* dout,
+    const float* dlast_state, void* du, void* ddelta, float* dA, void* dB,
+    void* dC, float* dD, void* dz, float* ddelta_bias, float* dinitial_state);
+
 #ifdef __cplusplus
 }
 #endif

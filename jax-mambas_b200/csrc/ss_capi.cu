@@ -80,6 +80,10 @@ BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
 
 }  // namespace
 
+namespace mss {
+mss_status set_error(mss_status code, const std::string& msg) { return fail(code, msg); }
+}  // namespace mss
+
 extern "C" {
 
 const char* mamba_ss_last_error(void) { return g_last_error.c_str(); }

@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <string>
+
 #include "ss_common.cuh"
 
 namespace mss {
@@ -17,6 +19,9 @@ cudaError_t launch_fwd(const FwdParams& p, int dstate, int io_dtype, int zoh,
 cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream);
+
+// Records `msg` as this host thread's mamba_ss_last_error() and returns code.
+mss_status set_error(mss_status code, const std::string& msg);
 
 // Returns and clears the forward kernel's device error word (0 = no error).
 unsigned int take_fwd_device_error();
