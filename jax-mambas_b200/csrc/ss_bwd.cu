@@ -15,17 +15,23 @@
 //      sum_n g a h_{t-1} A (-> ddelta), per lane dA, and the cross-channel
 //      sums dB = g delta u and dC = dy h in a shared-memory tile.
 // dz uses the pre-gate output y + D u saved by the forward.
-// dB/dC sum over the channels of a batch. The warps of a CTA (channels of one
-// batch) fold into one shared tile without atomics: at step s warp w works on
-// state (s + w*NS/G) mod NS, so no two warps touch one state row between the
-// barriers placed every NS/G steps. At the end of a chunk the tile is added
-// to the fp32 accumulators in global memory with 16-byte atomics.
+// The warps of a CTA (kBwdWarps channels of one batch) take the states in
+// lockstep. Each state's B and C rows for the chunk are staged once per CTA
+// by a 3-D tensor-map TMA copy whose 64-byte (fp32) / 32-byte (bf16) swizzle
+// makes every lane's 16-step run a conflict-free shared-memory read; the copy
+// of the next state flies while this one computes. dB/dC sum over channels:
+// each warp writes its rows to shared memory, the CTA adds the kBwdWarps rows
+// and adds the result to the fp32 accumulators in global memory with 16-byte
+// atomics.
 #include <algorithm>
+#include <cstring>
 
 #include "ss_common.cuh"
 #include "ss_launch.h"
 
 namespace mss {
+
+__device__ unsigned int g_bwd_device_error = 0;
 
 constexpr int kBwdWarps = 4;
 constexpr int kHalf = kItems / 2;
@@ -38,24 +44,70 @@ __device__ __forceinline__ int tile_slot(int q) {
   return (i << 2) | ((q & 3) ^ ((i >> 1) & 3));
 }
 
-template <int NS>
+// Tensor maps of the TMA-staged B and C (see launch_bwd).
+struct BwdMaps {
+  CUtensorMap b, c;
+};
+
+template <int NS, typename T>
 struct BwdShared {
-  static constexpr int G = NS < kBwdWarps ? NS : kBwdWarps;  // warps per copy
-  static constexpr int R = kBwdWarps / G;                    // tile copies
-  float4 accB[R][NS][kChunk / 4];
-  float4 accC[R][NS][kChunk / 4];
+  // one state's B and C for a chunk: 32 lane runs of kItems steps (swizzled)
+  alignas(1024) T bufB[2][32][kItems];
+  alignas(1024) T bufC[2][32][kItems];
+  // per-warp dB/dC rows of the current state, in tile_slot order
+  float4 wrow[2][kBwdWarps][2][kChunk / 4];
   float gcarry[kBwdWarps][NS];
   float dA[kBwdWarps][NS][32];
+  uint64_t bar[2];
 };
+
+// Staged B/C rows hold 32 lane runs of kItems steps. fp32 runs are 64 bytes
+// with the TMA's 64-byte swizzle (16-byte chunk j of run r sits at chunk
+// j ^ ((r >> 1) & 3)); bf16 runs are 32 bytes with the 32-byte swizzle
+// (chunk j at j ^ ((r >> 2) & 1)). Either way a warp reading one chunk per
+// lane touches every bank once.
+__device__ __forceinline__ int swz_chunk(int lane, int j, int esize) {
+  return esize == 4 ? (j ^ ((lane >> 1) & 3)) : (j ^ ((lane >> 2) & 1));
+}
+
+// Pairs 2j and 2j+1 (steps 4j .. 4j+3) of lane `lane`'s run.
+__device__ __forceinline__ void lds_quad(const float (*buf)[kItems], int lane, int j,
+                                         float2 (&v)[2]) {
+  const float4 f = *reinterpret_cast<const float4*>(buf[lane] + 4 * swz_chunk(lane, j, 4));
+  v[0] = make_float2(f.x, f.y);
+  v[1] = make_float2(f.z, f.w);
+}
+__device__ __forceinline__ void lds_quad(const __nv_bfloat16 (*buf)[kItems], int lane, int j,
+                                         float2 (&v)[2]) {
+  const uint2 w = *reinterpret_cast<const uint2*>(buf[lane] + 8 * swz_chunk(lane, j >> 1, 2) +
+                                                  4 * (j & 1));
+  v[0] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  v[1] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+}
+
+// Fills one state's staged B/C rows for the chunk at t0 with plain loads
+// (rows that TMA cannot serve), in the same swizzled layout; steps at or past
+// `len` read as zero. Called by the whole CTA.
+template <typename T>
+__device__ void stage_bc_plain(T (*bB)[kItems], T (*bC)[kItems], const T* Bn, const T* Cn,
+                               int t0, int len) {
+  for (int i = threadIdx.x; i < 2 * kChunk; i += blockDim.x) {
+    const int which = i / kChunk, k = i % kChunk;
+    const int t = t0 + k;
+    const T* src = which ? Cn : Bn;
+    const T v = t < len ? src[t] : T(0.f);
+    const int r = k / kItems, e = k % kItems;
+    constexpr int kPerChunk = 16 / sizeof(T);
+    const int pos = kPerChunk * swz_chunk(r, e / kPerChunk, sizeof(T)) + e % kPerChunk;
+    (which ? bC : bB)[r][pos] = v;
+  }
+}
 
 template <int NS, typename T, bool kZOH>
 __global__ void __launch_bounds__(kBwdWarps * 32, 3)
-    ss_bwd_kernel(const BwdParams p) {
-  using Sh = BwdShared<NS>;
-  constexpr int G = Sh::G;
-  constexpr int R = Sh::R;
-  constexpr int kPhase = NS / G;  // steps between barriers
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+    ss_bwd_kernel(const BwdParams p, const __grid_constant__ BwdMaps maps) {
+  using Sh = BwdShared<NS, T>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
 
   const int warp = threadIdx.x >> 5;
@@ -64,8 +116,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
   const int b = blockIdx.y;
   const bool active = d < p.dim;
   const int dc = active ? d : 0;  // clamp for parameter loads
-  const int copy = warp / G;
-  const int rot = (warp % G) * kPhase;
 
   const int L = p.seqlen;
   const size_t row = static_cast<size_t>(b) * p.dim + dc;
@@ -85,11 +135,25 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
   const float Dv = p.D ? __ldg(p.D + dc) : 0.f;
   const float bias = p.delta_bias ? __ldg(p.delta_bias + dc) : 0.f;
 
-  // Zero the tiles, seed the adjoint carries, clear the dA partials.
-  for (int i = threadIdx.x; i < R * NS * (kChunk / 4); i += blockDim.x) {
-    (&sh.accB[0][0][0])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    (&sh.accC[0][0][0])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const bool use_tma = p.tma_ok != 0;
+  // chunks at or past `len` are padding only and skipped; the TMA pipeline
+  // walks (chunk, state) for the others, chunks in reverse
+  const int c_first = len > 0 ? min(p.n_chunks - 1, (len - 1) / kChunk) : -1;
+  auto issue = [&](int c, int n, int seq) {  // one thread
+    uint64_t* bar = &sh.bar[seq & 1];
+    mbar_arrive_expect_tx(bar, 2u * 32u * kItems * sizeof(T));
+    const int y = c * (kChunk / kItems);
+    tma_load_3d(&sh.bufB[seq & 1][0][0], &maps.b, 0, y, b * NS + n, bar);
+    tma_load_3d(&sh.bufC[seq & 1][0][0], &maps.c, 0, y, b * NS + n, bar);
+  };
+  if (use_tma && threadIdx.x == 0) {
+    mbar_init(&sh.bar[0], 1);
+    mbar_init(&sh.bar[1], 1);
+    fence_mbar_init();
+    if (c_first >= 0) issue(c_first, 0, 0);
   }
+
+  // Seed the adjoint carries, clear the dA partials.
   if (lane < NS) {
     sh.gcarry[warp][lane] =
         (active && p.dlast) ? __ldg(p.dlast + row * NS + lane) : 0.f;
@@ -158,8 +222,27 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
     }
 
 #pragma unroll 1
-    for (int s = 0; s < NS; ++s) {
-      const int n = (s + rot) % NS;
+    for (int n = 0; n < NS; ++n) {
+      const int seq = (c_first - c) * NS + n;  // position in the TMA pipeline
+      const int sb = seq & 1;
+      if (use_tma) {
+        if (threadIdx.x == 0) {
+          const int nn = n + 1 < NS ? n + 1 : 0;
+          const int cn = n + 1 < NS ? c : c - 1;
+          if (cn >= 0) {
+            fence_proxy_async_smem();  // readers of that buffer passed a barrier
+            issue(cn, nn, seq + 1);
+          }
+        }
+        const bool ok = mbar_wait_bounded(&sh.bar[sb], (seq >> 1) & 1);
+        if (__syncthreads_or(!ok)) {
+          if (threadIdx.x == 0) {
+            atomicOr(&g_bwd_device_error, kErrTmaTimeout);
+            mbar_wait_bounded(&sh.bar[sb ^ 1], ((seq + 1) >> 1) & 1);
+          }
+          return;
+        }
+      }
       const float An = __ldg(p.A + dc * NS + n);
       const float2 a2 = dup2(An * kLog2e);
       const float2 A2 = dup2(An);
@@ -168,32 +251,42 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         hs = (p.h0 && active) ? __ldg(p.h0 + row * NS + n) : 0.f;
       else
         hs = active ? p.chunk_states[(row * p.n_chunks + c - 1) * NS + n] : 0.f;
-      const T* Bn = B_b + static_cast<size_t>(n) * L;
-      const T* Cn = C_b + static_cast<size_t>(n) * L;
-      float4* tileB = &sh.accB[copy][n][0];
-      float4* tileC = &sh.accC[copy][n][0];
+      float4* tileB = &sh.wrow[sb][warp][0][0];
+      float4* tileC = &sh.wrow[sb][warp][1][0];
+      if (!use_tma) {
+        // stage this state's B/C rows with plain loads, in the TMA's layout
+        stage_bc_plain(sh.bufB[sb], sh.bufC[sb], B_b + static_cast<size_t>(n) * L,
+                       C_b + static_cast<size_t>(n) * L, t0, len);
+        __syncthreads();
+      }
+      const T(*bB)[kItems] = sh.bufB[sb];
+      const T(*bC)[kItems] = sh.bufC[sb];
 
       // ---- forward recompute: a_t, and h_t for every step of the run
       float2 ab[kHalf], hv[kHalf];
       {
-        float2 Bv[kHalf];
-        load_run2(Bn, tl, lim, Bv);
         float H = 0.f;
 #pragma unroll
-        for (int i = 0; i < kHalf; ++i) {
-          const float2 arg = mul2(dl[i], a2);
-          ab[i] = make_float2(ex2(arg.x), ex2(arg.y));
-          float2 bu;
-          if constexpr (kZOH) {
-            const float inv = 1.f / An;
-            bu.x = Bv[i].x * (expm1f(dl[i].x * An) * inv) * duv[i].x;
-            bu.y = Bv[i].y * (expm1f(dl[i].y * An) * inv) * duv[i].y;
-          } else {
-            bu = mul2(Bv[i], duv[i]);
+        for (int j = 0; j < kHalf / 2; ++j) {
+          float2 Bq[2];
+          lds_quad(bB, lane, j, Bq);
+#pragma unroll
+          for (int ii = 0; ii < 2; ++ii) {
+            const int i = 2 * j + ii;
+            const float2 arg = mul2(dl[i], a2);
+            ab[i] = make_float2(ex2(arg.x), ex2(arg.y));
+            float2 bu;
+            if constexpr (kZOH) {
+              const float inv = 1.f / An;
+              bu.x = Bq[ii].x * (expm1f(dl[i].x * An) * inv) * duv[i].x;
+              bu.y = Bq[ii].y * (expm1f(dl[i].y * An) * inv) * duv[i].y;
+            } else {
+              bu = mul2(Bq[ii], duv[i]);
+            }
+            hv[i] = bu;  // b_t for now; h_t after the re-walk
+            H = fmaf(ab[i].x, H, bu.x);
+            H = fmaf(ab[i].y, H, bu.y);
           }
-          hv[i] = bu;  // b_t for now; h_t after the re-walk
-          H = fmaf(ab[i].x, H, bu.x);
-          H = fmaf(ab[i].y, H, bu.y);
         }
         float P = ex2(a2.x * ssum);
         warp_scan_fwd(P, H, lane);
@@ -211,37 +304,29 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         }
       }
 
-      // ---- dC = dy h (folded into the tile now) and e_t = dy_t C_t
-      float2 ev[kHalf];
-      {
-        float2 Cv[kHalf];
-        load_run2(Cn, tl, lim, Cv);
+      // ---- dC = dy h, written to this warp's row; local adjoint fold
+      float an_last = __shfl_down_sync(0xffffffffu, ab[0].x, 1);
+      if (lane == 31) an_last = 1.f;  // the carry already holds a_{t+1} g_{t+1}
+      float Gr = 0.f;
 #pragma unroll
-        for (int j = 0; j < kItems / 4; ++j) {
-          ev[2 * j] = mul2(dy[2 * j], Cv[2 * j]);
-          ev[2 * j + 1] = mul2(dy[2 * j + 1], Cv[2 * j + 1]);
-          const float2 c0 = mul2(dy[2 * j], hv[2 * j]);
-          const float2 c1 = mul2(dy[2 * j + 1], hv[2 * j + 1]);
-          float4& slot = tileC[tile_slot(lane * (kItems / 4) + j)];
-          const float4 v = slot;
-          const float2 lo = add2(make_float2(v.x, v.y), c0);
-          const float2 hi = add2(make_float2(v.z, v.w), c1);
-          slot = make_float4(lo.x, lo.y, hi.x, hi.y);
+      for (int j = kHalf / 2 - 1; j >= 0; --j) {
+        float2 Cq[2];
+        lds_quad(bC, lane, j, Cq);
+        const float2 c0 = mul2(dy[2 * j], hv[2 * j]);
+        const float2 c1 = mul2(dy[2 * j + 1], hv[2 * j + 1]);
+        tileC[tile_slot(lane * (kItems / 4) + j)] = make_float4(c0.x, c0.y, c1.x, c1.y);
+#pragma unroll
+        for (int ii = 1; ii >= 0; --ii) {
+          const int i = 2 * j + ii;
+          const float2 e = mul2(dy[i], Cq[ii]);  // e_t = dy_t C_t
+          Gr = fmaf(i == kHalf - 1 ? 0.f : ab[i + 1].x, Gr, e.y);
+          Gr = fmaf(ab[i].y, Gr, e.x);
         }
       }
 
       // ---- adjoint scan: g_t = e_t + a_{t+1} g_{t+1}
-      float an_last = __shfl_down_sync(0xffffffffu, ab[0].x, 1);
-      if (lane == 31) an_last = 1.f;  // the carry already holds a_{t+1} g_{t+1}
       float g;
       {
-        float Gr = ev[kHalf - 1].y;
-        Gr = fmaf(ab[kHalf - 1].y, Gr, ev[kHalf - 1].x);
-#pragma unroll
-        for (int i = kHalf - 2; i >= 0; --i) {
-          Gr = fmaf(ab[i + 1].x, Gr, ev[i].y);
-          Gr = fmaf(ab[i].y, Gr, ev[i].x);
-        }
         // lane map g_next -> Pr g_next + Gr with Pr = a_1 ... a_15 a_next
         float Pr = ex2(a2.x * ssum1) * an_last;
         warp_scan_rev(Pr, Gr, lane);
@@ -256,98 +341,80 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
 
       // ---- re-walk g backwards and form the gradient terms
       float2 dAl = make_float2(0.f, 0.f);
-      {
-        float2 Bv[kHalf];
-        load_run2(Bn, tl, lim, Bv);
-        float2 db_hi = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int i = kHalf - 1; i >= 0; --i) {
+      for (int j = kHalf / 2 - 1; j >= 0; --j) {
+        float2 Bq[2], Cq[2], dbp[2];
+        lds_quad(bB, lane, j, Bq);
+        lds_quad(bC, lane, j, Cq);
+#pragma unroll
+        for (int ii = 1; ii >= 0; --ii) {
+          const int i = 2 * j + ii;
+          const float2 e = mul2(dy[i], Cq[ii]);
           float2 gv;
-          gv.y = g = fmaf(i == kHalf - 1 ? an_last : ab[i + 1].x, g, ev[i].y);
-          gv.x = g = fmaf(ab[i].y, g, ev[i].x);
+          gv.y = g = fmaf(i == kHalf - 1 ? an_last : ab[i + 1].x, g, e.y);
+          gv.x = g = fmaf(ab[i].y, g, e.x);
           float2 bu, bb;
           if constexpr (kZOH) {
             const float inv = 1.f / An;
             bb.x = expm1f(dl[i].x * An) * inv;
             bb.y = expm1f(dl[i].y * An) * inv;
-            bu = mul2(mul2(Bv[i], bb), duv[i]);
+            bu = mul2(mul2(Bq[ii], bb), duv[i]);
           } else {
-            bu = mul2(Bv[i], duv[i]);
+            bu = mul2(Bq[ii], duv[i]);
           }
           // a_t h_{t-1} = h_t - b_t
           const float2 ah = add2(hv[i], make_float2(-bu.x, -bu.y));
           const float2 w = mul2(gv, ah);
           gA[i] = fma2(w, A2, gA[i]);
           dAl = fma2(w, dl[i], dAl);
-          float2 db;
           if constexpr (kZOH) {
             // d b_t/d delta = a_t B u, d b_t/d A = B u (delta a_t - b_bar) / A
-            const float2 gBu = mul2(gv, mul2(Bv[i], duv[i]));
+            const float2 gBu = mul2(gv, mul2(Bq[ii], duv[i]));
             gA[i] = fma2(gBu, ab[i], gA[i]);
             const float inv = 1.f / An;
             dAl.x += gBu.x * (dl[i].x * ab[i].x - bb.x) * inv;
             dAl.y += gBu.y * (dl[i].y * ab[i].y - bb.y) * inv;
-            gB[i] = fma2(gv, mul2(Bv[i], bb), gB[i]);
-            db = mul2(gv, mul2(bb, duv[i]));
+            gB[i] = fma2(gv, mul2(Bq[ii], bb), gB[i]);
+            dbp[ii] = mul2(gv, mul2(bb, duv[i]));
           } else {
-            gB[i] = fma2(gv, Bv[i], gB[i]);
-            db = mul2(gv, duv[i]);
-          }
-          if (i & 1) {
-            db_hi = db;
-          } else {
-            float4& slot = tileB[tile_slot(lane * (kItems / 4) + (i >> 1))];
-            const float4 v = slot;
-            const float2 lo = add2(make_float2(v.x, v.y), db);
-            const float2 hi = add2(make_float2(v.z, v.w), db_hi);
-            slot = make_float4(lo.x, lo.y, hi.x, hi.y);
+            gB[i] = fma2(gv, Bq[ii], gB[i]);
+            dbp[ii] = mul2(gv, duv[i]);
           }
         }
+        tileB[tile_slot(lane * (kItems / 4) + j)] =
+            make_float4(dbp[0].x, dbp[0].y, dbp[1].x, dbp[1].y);
       }
       const float gnext = __shfl_sync(0xffffffffu, ab[0].x * g, 0);
       if (lane == 0) sh.gcarry[warp][n] = gnext;
       sh.dA[warp][n][lane] += dAl.x + dAl.y;
-      if ((s + 1) % kPhase == 0) __syncthreads();
-    }
+      __syncthreads();
 
-    // ---- flush the dB/dC tiles of this chunk into global fp32 accumulators
-    {
-      const size_t base = static_cast<size_t>(b) * NS * L;
-      for (int q = threadIdx.x; q < NS * (kChunk / 4); q += blockDim.x) {
-        const int n = q / (kChunk / 4);
-        const int qq = q % (kChunk / 4);
-        const int slot = tile_slot(qq);
-        float4 vb = make_float4(0.f, 0.f, 0.f, 0.f), vc = vb;
+      // ---- add the warps' dB/dC rows of this state into the fp32 accumulators
+      {
+        const size_t base = (static_cast<size_t>(b) * NS + n) * L;
+        for (int q = threadIdx.x; q < 2 * (kChunk / 4); q += blockDim.x) {
+          const int which = q / (kChunk / 4);  // 0: dB, 1: dC
+          const int qq = q % (kChunk / 4);
+          const int slot = tile_slot(qq);
+          float4 v = sh.wrow[sb][0][which][slot];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float4 xb = sh.accB[r][n][slot];
-          const float4 xc = sh.accC[r][n][slot];
-          vb.x += xb.x; vb.y += xb.y; vb.z += xb.z; vb.w += xb.w;
-          vc.x += xc.x; vc.y += xc.y; vc.z += xc.z; vc.w += xc.w;
-          sh.accB[r][n][slot] = make_float4(0.f, 0.f, 0.f, 0.f);
-          sh.accC[r][n][slot] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        const int t = t0 + qq * 4;
-        if (t >= len) continue;
-        float* gb = p.dB_acc + base + static_cast<size_t>(n) * L + t;
-        float* gc = p.dC_acc + base + static_cast<size_t>(n) * L + t;
-        if (t + 4 <= len && ((reinterpret_cast<uintptr_t>(gb) & 15) == 0) &&
-            ((reinterpret_cast<uintptr_t>(gc) & 15) == 0)) {
-          atomicAdd(reinterpret_cast<float4*>(gb), vb);
-          atomicAdd(reinterpret_cast<float4*>(gc), vc);
-        } else {
-          const float eb[4] = {vb.x, vb.y, vb.z, vb.w};
-          const float ec[4] = {vc.x, vc.y, vc.z, vc.w};
+          for (int w = 1; w < kBwdWarps; ++w) {
+            const float4 x = sh.wrow[sb][w][which][slot];
+            v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+          }
+          const int t = t0 + qq * 4;
+          if (t >= len) continue;
+          float* gp = (which ? p.dC_acc : p.dB_acc) + base + t;
+          if (t + 4 <= len && ((reinterpret_cast<uintptr_t>(gp) & 15) == 0)) {
+            atomicAdd(reinterpret_cast<float4*>(gp), v);
+          } else {
+            const float e4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (t + e < len) {
-              atomicAdd(gb + e, eb[e]);
-              atomicAdd(gc + e, ec[e]);
-            }
+            for (int e = 0; e < 4; ++e)
+              if (t + e < len) atomicAdd(gp + e, e4[e]);
           }
         }
       }
-      __syncthreads();
     }
 
     // ---- per-step epilogue
@@ -453,28 +520,47 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src,
 }
 
 template <int NS, typename T, bool kZOH>
-static cudaError_t launch_bwd_t(const BwdParams& p, cudaStream_t stream) {
-  const size_t smem = sizeof(BwdShared<NS>);
+static cudaError_t launch_bwd_t(const BwdParams& p, const BwdMaps& maps,
+                                cudaStream_t stream) {
+  const size_t smem = sizeof(BwdShared<NS, T>);
   auto kern = ss_bwd_kernel<NS, T, kZOH>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   dim3 grid((p.dim + kBwdWarps - 1) / kBwdWarps, p.batch);
-  kern<<<grid, kBwdWarps * 32, smem, stream>>>(p);
+  kern<<<grid, kBwdWarps * 32, smem, stream>>>(p, maps);
   return cudaPeekAtLastError();
 }
 
 template <typename T, bool kZOH>
-static cudaError_t launch_bwd_n(const BwdParams& p, int dstate,
+static cudaError_t launch_bwd_n(const BwdParams& p, const BwdMaps& maps, int dstate,
                                 cudaStream_t stream) {
   switch (dstate) {
-    case 1: return launch_bwd_t<1, T, kZOH>(p, stream);
-    case 2: return launch_bwd_t<2, T, kZOH>(p, stream);
-    case 4: return launch_bwd_t<4, T, kZOH>(p, stream);
-    case 8: return launch_bwd_t<8, T, kZOH>(p, stream);
-    case 16: return launch_bwd_t<16, T, kZOH>(p, stream);
+    case 1: return launch_bwd_t<1, T, kZOH>(p, maps, stream);
+    case 2: return launch_bwd_t<2, T, kZOH>(p, maps, stream);
+    case 4: return launch_bwd_t<4, T, kZOH>(p, maps, stream);
+    case 8: return launch_bwd_t<8, T, kZOH>(p, maps, stream);
+    case 16: return launch_bwd_t<16, T, kZOH>(p, maps, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// B or C (batch*dstate rows of L) as a 3-D tensor [rows][L/kItems][kItems]
+// with boxes of one row x 32 runs x kItems, swizzled so that each lane's run
+// is a conflict-free 16-byte-chunk read.
+static bool encode_bc(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
+                      uint64_t L) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kItems), L / kItems, rows};
+  const cuuint64_t strides[2] = {kItems * esize, L * esize};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kItems), 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, io_dtype == MSS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+            3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            io_dtype == MSS_BF16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
@@ -486,12 +572,23 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
   e = cudaMemsetAsync(p.dC_acc, 0, n_bnl * sizeof(float), stream);
   if (e != cudaSuccess) return e;
 
+  BwdParams pk = p;
+  BwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
+  const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  pk.tma_ok = p.seqlen % kItems == 0 && (p.seqlen * esize) % 16 == 0 && al16(p.B) && al16(p.C);
+  if (pk.tma_ok) {
+    const uint64_t rows = static_cast<uint64_t>(p.batch) * dstate;
+    pk.tma_ok = encode_bc(&maps.b, p.B, io_dtype, rows, p.seqlen) &&
+                encode_bc(&maps.c, p.C, io_dtype, rows, p.seqlen);
+  }
   if (io_dtype == MSS_BF16) {
-    e = zoh ? launch_bwd_n<__nv_bfloat16, true>(p, dstate, stream)
-            : launch_bwd_n<__nv_bfloat16, false>(p, dstate, stream);
+    e = zoh ? launch_bwd_n<__nv_bfloat16, true>(pk, maps, dstate, stream)
+            : launch_bwd_n<__nv_bfloat16, false>(pk, maps, dstate, stream);
   } else {
-    e = zoh ? launch_bwd_n<float, true>(p, dstate, stream)
-            : launch_bwd_n<float, false>(p, dstate, stream);
+    e = zoh ? launch_bwd_n<float, true>(pk, maps, dstate, stream)
+            : launch_bwd_n<float, false>(pk, maps, dstate, stream);
   }
   if (e != cudaSuccess) return e;
 
@@ -516,6 +613,13 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
     e = cudaPeekAtLastError();
   }
   return e;
+}
+
+unsigned int take_bwd_device_error() {
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_bwd_device_error, sizeof(v)) != cudaSuccess) return ~0u;
+  cudaMemcpyToSymbol(g_bwd_device_error, &zero, sizeof(zero));
+  return v;
 }
 
 }  // namespace mss

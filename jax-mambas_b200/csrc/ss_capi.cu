@@ -90,7 +90,9 @@ const char* mamba_ss_last_error(void) { return g_last_error.c_str(); }
 
 const char* mamba_ss_version(void) { return "mamba-ss-b200 0.1 sm_100a"; }
 
-uint32_t mamba_ss_take_device_error(void) { return mss::take_fwd_device_error(); }
+uint32_t mamba_ss_take_device_error(void) {
+  return mss::take_fwd_device_error() | mss::take_bwd_device_error();
+}
 
 int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
                                     int32_t dstate) {

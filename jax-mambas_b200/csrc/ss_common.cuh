@@ -49,6 +49,7 @@ struct FwdParams {
 struct BwdParams {
   int batch, dim, seqlen, n_chunks;
   int delta_softplus;
+  int tma_ok;  // B/C may be staged with TMA (set by the launcher)
   const void* u;
   const void* delta;
   const void* z;
@@ -265,6 +266,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 3-D TMA tile copy global -> shared (coordinates innermost first).
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 

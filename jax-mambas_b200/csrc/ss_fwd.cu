@@ -443,8 +443,7 @@ static int fwd_channels_per_cta(int dstate) {
   }
 }
 
-// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     cudaDriverEntryPointQueryResult q;
@@ -460,7 +459,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Row-major [rows][L] tensor, boxes of [box_rows][kTile]; zero fill outside.
 static bool encode_rows(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
                         uint64_t L, uint32_t box_rows, bool swizzle128 = false) {
-  auto fn = encode_fn();
+  auto fn = tensor_map_encoder();
   if (!fn) return false;
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
   const cuuint64_t dims[2] = {L, rows};

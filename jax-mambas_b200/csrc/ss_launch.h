@@ -1,6 +1,7 @@
 // Host-side launchers shared by the C ABI (ss_capi.cu).
 #pragma once
 
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <string>
@@ -23,7 +24,11 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
 // Records `msg` as this host thread's mamba_ss_last_error() and returns code.
 mss_status set_error(mss_status code, const std::string& msg);
 
-// Returns and clears the forward kernel's device error word (0 = no error).
+// Returns and clears the forward / backward kernels' device error words.
 unsigned int take_fwd_device_error();
+unsigned int take_bwd_device_error();
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 }  // namespace mss
