@@ -71,7 +71,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100", "-f", self.path],
+                 "--format=csv,noheader,nounits", "-lms", "50", "-f", self.path],
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -134,6 +134,7 @@ def run_gpu(args, cfg):
     import torch.distributed as dist
 
     from mamba import selective_scan_cuda as ssc
+    from mamba.distributed import allreduce_param_grads, flat_param_grads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -171,8 +172,7 @@ def run_gpu(args, cfg):
     cs = torch.empty(ssc.chunk_states_elems(b, L, d, n), device=dev)
     du, ddl, dz = torch.empty_like(u), torch.empty_like(u), torch.empty_like(u)
     dB, dC = torch.empty_like(Bm), torch.empty_like(Cm)
-    params = torch.empty(d * n + 2 * d, device=dev)  # dA | dD | dbias (one all-reduce)
-    dA, dDp, dbias = params[: d * n].view(d, n), params[d * n: d * n + d], params[d * n + d:]
+    params, dA, dDp, dbias = flat_param_grads(d, n, dev)  # one all-reduce buffer
     ws = ssc._alloc_workspace(b, L, d, n, 1 if io == torch.bfloat16 else 0, dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -188,8 +188,7 @@ def run_gpu(args, cfg):
     def step():
         fwd()
         bwd()
-        if world > 1:
-            dist.all_reduce(params)
+        allreduce_param_grads(params)
 
     for _ in range(max(args.warmup, 0)):
         step()
@@ -210,8 +209,7 @@ def run_gpu(args, cfg):
             ev[i][1].record(stream)
             bwd()
             ev[i][2].record(stream)
-            if world > 1:
-                dist.all_reduce(params)
+            allreduce_param_grads(params)
         t_end.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -227,6 +225,12 @@ def run_gpu(args, cfg):
         total_ms = float(t.item())
 
     elems, fwd_bytes, bwd_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize)
+    # padded steps are skipped by the kernels: the rooflines count
+    # the valid steps only, the headline value counts every B*D*L position
+    valid = 1.0
+    if seq_lens is not None:
+        valid = float(seq_lens.sum().item()) / (b * L)
+    fwd_bytes, bwd_bytes = fwd_bytes * valid, bwd_bytes * valid
     ms_per_step = total_ms / args.steps
     value = elems * world / (ms_per_step * 1e-3) / 1e9
 
@@ -243,8 +247,13 @@ def run_gpu(args, cfg):
     fwd_gbs = fwd_bytes / (fwd_ms * 1e-3) / 1e9
     f_mhz = clocks.get("sm_mhz") or sm_max
     mufu_peak = 148 * 16 * f_mhz * 1e6  # ops/s: 16 MUFU lanes per SM per clock
-    mufu_bwd = elems * mufu_b / (bwd_ms * 1e-3)
-    mufu_fwd = elems * mufu_f / (fwd_ms * 1e-3)
+    mufu_bwd = elems * valid * mufu_b / (bwd_ms * 1e-3)
+    mufu_fwd = elems * valid * mufu_f / (fwd_ms * 1e-3)
+    traffic = args.traffic
+    if traffic is None and args.config == "c1":
+        tf = ROOT / "profiles" / "ncu_traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("c1", {}).get("ss_bwd_kernel")
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -254,11 +263,12 @@ def run_gpu(args, cfg):
                    "dstate": n, "global_batch": b * world,
                    "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (u, delta, z, dy: "
-                         f"{elems * esize * 4 / 1e6:.0f} MB per step)"},
+                         f"{elems * esize * 4 / 1e6:.0f} MB per step)",
+                   "valid_fraction": round(valid, 4)},
         "kernels_ms": {"fwd": round(fwd_ms, 4), "bwd": round(bwd_ms, 4)},
         "roofline": {"bound": "hbm", "kernel": "ss_bwd_kernel",
                      "achieved": round(bwd_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(bwd_gbs / hbm, 4), "traffic": args.traffic,
+                     "frac": round(bwd_gbs / hbm, 4), "traffic": traffic,
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_src == "measured" else "fallback 6.65 TB/s",
                      "algorithmic_bytes_per_launch": bwd_bytes},
@@ -440,7 +450,7 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
