@@ -46,7 +46,9 @@ __device__ __forceinline__ int tile_slot(int q) {
 
 // Tensor maps of the TMA-staged B and C (see launch_bwd).
 struct BwdMaps {
-  CUtensorMap b, c;
+  CUtensorMap b, c;                    // [rows = batch*dstate][L/16][16]
+  CUtensorMap u, d, z, dout, pre;      // [rows = batch*dim][L/16][16], loads
+  CUtensorMap du, dd, dz;              // same shape, stores
 };
 
 template <int NS, typename T>
@@ -54,12 +56,26 @@ struct BwdShared {
   // one state's B and C for a chunk: 32 lane runs of kItems steps (swizzled)
   alignas(1024) T bufB[2][32][kItems];
   alignas(1024) T bufC[2][32][kItems];
-  // per-warp dB/dC rows of the current state, in tile_slot order
-  float4 wrow[2][kBwdWarps][2][kChunk / 4];
+  // this chunk's u and delta runs per warp (swizzled like B/C); reused to
+  // stage du and ddelta for the TMA stores
+  alignas(1024) T arrU[kBwdWarps][32][kItems];
+  alignas(1024) T arrD[kBwdWarps][32][kItems];
+  // per-warp dB/dC rows of the current state, in tile_slot order. Before the
+  // state loop the same bytes hold the chunk's z, dout and pre-gate runs
+  // (zone offsets 0, kArr and 16 KiB); dz is staged in the pre-gate slot,
+  // which lies in the half used from the second state on.
+  alignas(1024) float4 wrow[2][kBwdWarps][2][kChunk / 4];
   float gcarry[kBwdWarps][NS];
   float dA[kBwdWarps][NS][32];
-  uint64_t bar[2];
+  uint64_t bar[3];
+  static constexpr int kArr = kBwdWarps * 32 * kItems;  // elements per chunk array
+  __device__ T (*zone(int k))[32][kItems] {
+    unsigned char* base = reinterpret_cast<unsigned char*>(&wrow[0][0][0][0]);
+    const size_t off = k == 0 ? 0 : k == 1 ? kArr * sizeof(T) : 16384;
+    return reinterpret_cast<T(*)[32][kItems]>(base + off);
+  }
 };
+static_assert(3 * 4 * 32 * kItems * 4 <= 2 * 4 * 2 * (kChunk / 4) * 16, "zone fits wrow");
 
 // Staged B/C rows hold 32 lane runs of kItems steps. fp32 runs are 64 bytes
 // with the TMA's 64-byte swizzle (16-byte chunk j of run r sits at chunk
@@ -83,6 +99,36 @@ __device__ __forceinline__ void lds_quad(const __nv_bfloat16 (*buf)[kItems], int
                                                   4 * (j & 1));
   v[0] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
   v[1] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+}
+
+template <typename T>
+__device__ __forceinline__ void lds_run16(const T (*buf)[kItems], int lane,
+                                          float2 (&v)[kItems / 2]) {
+#pragma unroll
+  for (int j = 0; j < kItems / 4; ++j) {
+    float2 q[2];
+    lds_quad(buf, lane, j, q);
+    v[2 * j] = q[0];
+    v[2 * j + 1] = q[1];
+  }
+}
+
+__device__ __forceinline__ void sts_quad(float (*buf)[kItems], int lane, int j, float2 a,
+                                         float2 b) {
+  *reinterpret_cast<float4*>(buf[lane] + 4 * swz_chunk(lane, j, 4)) = make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void sts_quad(__nv_bfloat16 (*buf)[kItems], int lane, int j,
+                                         float2 a, float2 b) {
+  uint2 w;
+  *reinterpret_cast<__nv_bfloat162*>(&w.x) = __floats2bfloat162_rn(a.x, a.y);
+  *reinterpret_cast<__nv_bfloat162*>(&w.y) = __floats2bfloat162_rn(b.x, b.y);
+  *reinterpret_cast<uint2*>(buf[lane] + 8 * swz_chunk(lane, j >> 1, 2) + 4 * (j & 1)) = w;
+}
+template <typename T>
+__device__ __forceinline__ void sts_run16(T (*buf)[kItems], int lane,
+                                          const float2 (&v)[kItems / 2]) {
+#pragma unroll
+  for (int j = 0; j < kItems / 4; ++j) sts_quad(buf, lane, j, v[2 * j], v[2 * j + 1]);
 }
 
 // Fills one state's staged B/C rows for the chunk at t0 with plain loads
@@ -146,9 +192,14 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
     tma_load_3d(&sh.bufB[seq & 1][0][0], &maps.b, 0, y, b * NS + n, bar);
     tma_load_3d(&sh.bufC[seq & 1][0][0], &maps.c, 0, y, b * NS + n, bar);
   };
+  // TMA stores write whole boxes of kBwdWarps rows: only CTAs whose rows all
+  // belong to this batch may use them (a tail CTA would spill into the next).
+  const bool tma_store = use_tma && (blockIdx.x + 1) * kBwdWarps <= p.dim;
+  const int row0 = b * p.dim + blockIdx.x * kBwdWarps;  // first (batch, channel) row
   if (use_tma && threadIdx.x == 0) {
     mbar_init(&sh.bar[0], 1);
     mbar_init(&sh.bar[1], 1);
+    mbar_init(&sh.bar[2], 1);
     fence_mbar_init();
     if (c_first >= 0) issue(c_first, 0, 0);
   }
@@ -181,37 +232,103 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       continue;
     }
 
-    // ---- per-step inputs of this lane's run
+    // ---- stage this chunk's u, delta, dout, z and pre-gate runs
+    const int ycoord = c * (kChunk / kItems);
+    if (use_tma) {
+      if (threadIdx.x == 0) {
+        bulk_wait_read_all();  // the previous chunk's du/ddelta stores left smem
+        fence_proxy_async_smem();  // and the CTA's reads of those buffers are done
+        const uint32_t blk = Sh::kArr * sizeof(T);
+        mbar_arrive_expect_tx(&sh.bar[2], (z_row ? 5u : 3u) * blk);
+        tma_load_3d(&sh.arrU[0][0][0], &maps.u, 0, ycoord, row0, &sh.bar[2]);
+        tma_load_3d(&sh.arrD[0][0][0], &maps.d, 0, ycoord, row0, &sh.bar[2]);
+        tma_load_3d(&sh.zone(1)[0][0][0], &maps.dout, 0, ycoord, row0, &sh.bar[2]);
+        if (z_row) {
+          tma_load_3d(&sh.zone(0)[0][0][0], &maps.z, 0, ycoord, row0, &sh.bar[2]);
+          tma_load_3d(&sh.zone(2)[0][0][0], &maps.pre, 0, ycoord, row0, &sh.bar[2]);
+        }
+      }
+      const bool ok = mbar_wait_bounded(&sh.bar[2], (c_first - c) & 1);
+      if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0) {
+          atomicOr(&g_bwd_device_error, kErrTmaTimeout);
+          mbar_wait_bounded(&sh.bar[(c_first - c) * NS & 1], (((c_first - c) * NS) >> 1) & 1);
+          bulk_wait_all();
+        }
+        return;
+      }
+    } else {
+      float2 v[kHalf];
+      load_run2(u_row, tl, lim, v);
+      sts_run16(sh.arrU[warp], lane, v);
+      load_run2(dl_row, tl, lim, v);
+      sts_run16(sh.arrD[warp], lane, v);
+      load_run2(dout_row, tl, lim, v);
+      sts_run16(sh.zone(1)[warp], lane, v);
+      if (z_row) {
+        load_run2(z_row, tl, lim, v);
+        sts_run16(sh.zone(0)[warp], lane, v);
+        load_run2(static_cast<const T*>(p.out_pre) + row * L, tl, lim, v);
+        sts_run16(sh.zone(2)[warp], lane, v);
+      }
+      __syncwarp();
+    }
+
+    // ---- per-step inputs of this lane's run; dz (independent of the scan)
     float2 dl[kHalf], duv[kHalf], dy[kHalf];
     float ssum, ssum1;  // sum of delta over the run, and without its first step
     {
       float2 uv[kHalf];
-      load_run2(u_row, tl, lim, uv);
-      load_run2(dl_row, tl, lim, dl);
-      load_run2(dout_row, tl, lim, dy);
+      lds_run16(sh.arrU[warp], lane, uv);
+      lds_run16(sh.arrD[warp], lane, dl);
+      lds_run16(sh.zone(1)[warp], lane, dy);
       if (z_row) {
-        float2 zv[kHalf];
-        load_run2(z_row, tl, lim, zv);
+        // dz = dout * (y + D u) * silu'(z), with y + D u saved by the forward
+        float2 zv[kHalf], pv[kHalf], dzv[kHalf];
+        lds_run16(sh.zone(0)[warp], lane, zv);
+        lds_run16(sh.zone(2)[warp], lane, pv);
 #pragma unroll
         for (int i = 0; i < kHalf; ++i) {
-          dy[i].x *= silu_f(zv[i].x);
-          dy[i].y *= silu_f(zv[i].y);
+          const float s0 = sigmoid_f(zv[i].x), s1 = sigmoid_f(zv[i].y);
+          const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
+          dzv[i].x = v0 ? dy[i].x * pv[i].x * s0 * fmaf(zv[i].x, 1.f - s0, 1.f) : 0.f;
+          dzv[i].y = v1 ? dy[i].y * pv[i].y * s1 * fmaf(zv[i].y, 1.f - s1, 1.f) : 0.f;
+          dy[i].x *= zv[i].x * s0;
+          dy[i].y *= zv[i].y * s1;
+        }
+        if (tma_store) {
+          sts_run16(sh.zone(2)[warp], lane, dzv);
+        } else if (active) {
+          store_run2(dz_row, tl, L, dzv);
         }
       }
       ssum = 0.f;
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) {
-        float v0 = dl[i].x + bias, v1 = dl[i].y + bias;
+        const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
+        float x0 = dl[i].x + bias, x1 = dl[i].y + bias;
         if (p.delta_softplus) {
-          v0 = softplus_f(v0);
-          v1 = softplus_f(v1);
+          x0 = softplus_f(x0);
+          x1 = softplus_f(x1);
         }
-        dl[i].x = (tl + 2 * i < lim) ? v0 : 0.f;
-        dl[i].y = (tl + 2 * i + 1 < lim) ? v1 : 0.f;
+        dl[i].x = v0 ? x0 : 0.f;
+        dl[i].y = v1 ? x1 : 0.f;
+        uv[i].x = v0 ? uv[i].x : 0.f;
+        uv[i].y = v1 ? uv[i].y : 0.f;
+        dy[i].x = v0 ? dy[i].x : 0.f;
+        dy[i].y = v1 ? dy[i].y : 0.f;
         ssum += dl[i].x + dl[i].y;
         duv[i] = kZOH ? uv[i] : mul2(dl[i], uv[i]);
       }
       ssum1 = ssum - dl[0].x;
+    }
+    if (z_row && tma_store) {
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        tma_store_3d(&maps.dz, 0, ycoord, row0, &sh.zone(2)[0][0][0]);
+        bulk_commit();
+      }
     }
 
     float2 gA[kHalf], gB[kHalf];
@@ -387,6 +504,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       const float gnext = __shfl_sync(0xffffffffu, ab[0].x * g, 0);
       if (lane == 0) sh.gcarry[warp][n] = gnext;
       sh.dA[warp][n][lane] += dAl.x + dAl.y;
+      if (n == 0 && threadIdx.x == 0 && z_row && tma_store)
+        bulk_wait_read_all();  // dz left the zone before wrow[1] is written
       __syncthreads();
 
       // ---- add the warps' dB/dC rows of this state into the fp32 accumulators
@@ -417,14 +536,17 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       }
     }
 
-    // ---- per-step epilogue
-    if (active) {
+    // ---- per-step epilogue: du, ddelta (dz was written before the scan)
+    {
       float2 uv[kHalf], dv[kHalf];
-      load_run2(u_row, tl, lim, uv);
-      load_run2(dl_row, tl, lim, dv);
+      lds_run16(sh.arrU[warp], lane, uv);
+      lds_run16(sh.arrD[warp], lane, dv);
       float2 o_du[kHalf], o_dd[kHalf];
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) {
+        const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
+        uv[i].x = v0 ? uv[i].x : 0.f;
+        uv[i].y = v1 ? uv[i].y : 0.f;
         // ddelta_eff = sum_n g (B u + a h_{t-1} A)   (Euler; ZOH: gA holds all)
         float2 gd = kZOH ? gA[i] : fma2(uv[i], gB[i], gA[i]);
         if (p.delta_softplus) {
@@ -433,7 +555,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         }
         const float2 gu = kZOH ? gB[i] : mul2(dl[i], gB[i]);
         float2 du_ = fma2(dup2(Dv), dy[i], gu);
-        const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
         gd.x = v0 ? gd.x : 0.f;
         gd.y = v1 ? gd.y : 0.f;
         du_.x = v0 ? du_.x : 0.f;
@@ -443,24 +564,26 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         dD_acc = fmaf(dy[i].x, uv[i].x, fmaf(dy[i].y, uv[i].y, dD_acc));
         dbias_acc += gd.x + gd.y;
       }
-      store_run2(du_row, tl, L, o_du);
-      store_run2(ddl_row, tl, L, o_dd);
-      if (dz_row) {
-        // dz = dout * (y + D u) * silu'(z), with y + D u saved by the forward
-        float2 zv[kHalf], dov[kHalf], pv[kHalf], o_dz[kHalf];
-        load_run2(z_row, tl, lim, zv);
-        load_run2(dout_row, tl, lim, dov);
-        load_run2(static_cast<const T*>(p.out_pre) + row * L, tl, lim, pv);
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) {
-          const float s0 = sigmoid_f(zv[i].x), s1 = sigmoid_f(zv[i].y);
-          o_dz[i].x = dov[i].x * pv[i].x * s0 * fmaf(zv[i].x, 1.f - s0, 1.f);
-          o_dz[i].y = dov[i].y * pv[i].y * s1 * fmaf(zv[i].y, 1.f - s1, 1.f);
+      if (tma_store) {
+        sts_run16(sh.arrU[warp], lane, o_du);
+        sts_run16(sh.arrD[warp], lane, o_dd);
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          tma_store_3d(&maps.du, 0, ycoord, row0, &sh.arrU[0][0][0]);
+          tma_store_3d(&maps.dd, 0, ycoord, row0, &sh.arrD[0][0][0]);
+          bulk_commit();
         }
-        store_run2(dz_row, tl, L, o_dz);
+      } else {
+        if (active) {
+          store_run2(du_row, tl, L, o_du);
+          store_run2(ddl_row, tl, L, o_dd);
+        }
+        __syncthreads();  // arrU/arrD are refilled by the next chunk
       }
     }
   }
+  if (use_tma && threadIdx.x == 0) bulk_wait_all();
 
   // ---- per-row results
   dD_acc = warp_sum(dD_acc);
@@ -545,17 +668,18 @@ static cudaError_t launch_bwd_n(const BwdParams& p, const BwdMaps& maps, int dst
   }
 }
 
-// B or C (batch*dstate rows of L) as a 3-D tensor [rows][L/kItems][kItems]
-// with boxes of one row x 32 runs x kItems, swizzled so that each lane's run
-// is a conflict-free 16-byte-chunk read.
-static bool encode_bc(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
-                      uint64_t L) {
+// A (rows x L) operand as a 3-D tensor [rows][L/kItems][kItems], in boxes of
+// box_rows rows x 32 runs x kItems steps, swizzled so that each lane's run is
+// a conflict-free 16-byte-chunk read (64-byte swizzle for fp32 runs, 32-byte
+// for bf16).
+static bool encode_runs(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
+                        uint64_t L, uint32_t box_rows) {
   auto fn = tensor_map_encoder();
   if (!fn) return false;
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kItems), L / kItems, rows};
   const cuuint64_t strides[2] = {kItems * esize, L * esize};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kItems), 32, 1};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kItems), 32, box_rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, io_dtype == MSS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
             3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -577,11 +701,23 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
   memset(&maps, 0, sizeof(maps));
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
   const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  pk.tma_ok = p.seqlen % kItems == 0 && (p.seqlen * esize) % 16 == 0 && al16(p.B) && al16(p.C);
+  pk.tma_ok = p.seqlen % kItems == 0 && (p.seqlen * esize) % 16 == 0 && al16(p.B) &&
+              al16(p.C) && al16(p.u) && al16(p.delta) && al16(p.dout) && al16(p.du) &&
+              al16(p.ddelta) && (!p.z || (al16(p.z) && al16(p.dz) && al16(p.out_pre)));
   if (pk.tma_ok) {
-    const uint64_t rows = static_cast<uint64_t>(p.batch) * dstate;
-    pk.tma_ok = encode_bc(&maps.b, p.B, io_dtype, rows, p.seqlen) &&
-                encode_bc(&maps.c, p.C, io_dtype, rows, p.seqlen);
+    const uint64_t brows = static_cast<uint64_t>(p.batch) * dstate;
+    const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
+    const uint64_t L = p.seqlen;
+    pk.tma_ok = encode_runs(&maps.b, p.B, io_dtype, brows, L, 1) &&
+                encode_runs(&maps.c, p.C, io_dtype, brows, L, 1) &&
+                encode_runs(&maps.u, p.u, io_dtype, rows, L, kBwdWarps) &&
+                encode_runs(&maps.d, p.delta, io_dtype, rows, L, kBwdWarps) &&
+                encode_runs(&maps.dout, p.dout, io_dtype, rows, L, kBwdWarps) &&
+                encode_runs(&maps.du, p.du, io_dtype, rows, L, kBwdWarps) &&
+                encode_runs(&maps.dd, p.ddelta, io_dtype, rows, L, kBwdWarps) &&
+                (!p.z || (encode_runs(&maps.z, p.z, io_dtype, rows, L, kBwdWarps) &&
+                          encode_runs(&maps.pre, p.out_pre, io_dtype, rows, L, kBwdWarps) &&
+                          encode_runs(&maps.dz, p.dz, io_dtype, rows, L, kBwdWarps)));
   }
   if (io_dtype == MSS_BF16) {
     e = zoh ? launch_bwd_n<__nv_bfloat16, true>(pk, maps, dstate, stream)
