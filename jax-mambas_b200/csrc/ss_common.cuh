@@ -216,6 +216,13 @@ __device__ __forceinline__ float sigmoid_f(float x) {
 
 __device__ __forceinline__ float silu_f(float z) { return z * sigmoid_f(z); }
 
+// sigmoid(x) from s = softplus(x): 1 - e^{-s}; for small s the series
+// s (1 - s/2 (1 - s/3 (1 - s/4))) avoids the cancellation of 1 - e^{-s}.
+__device__ __forceinline__ float sigmoid_from_softplus(float s) {
+  const float series = s * fmaf(-0.5f * s, fmaf(-s * (1.f / 3.f), fmaf(-0.25f, s, 1.f), 1.f), 1.f);
+  return s < 0.0625f ? series : 1.f - ex2(-s * kLog2e);
+}
+
 // ------------------------------------------------- TMA bulk copies, mbarriers
 __device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
