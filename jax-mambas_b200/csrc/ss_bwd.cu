@@ -435,6 +435,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       float an_last = __shfl_down_sync(0xffffffffu, ab[0].x, 1);
       if (lane == 31) an_last = 1.f;  // the carry already holds a_{t+1} g_{t+1}
       float Gr = 0.f;
+      float2 ev[kHalf];  // e_t = dy_t C_t, kept for the re-walk
 #pragma unroll
       for (int j = kHalf / 2 - 1; j >= 0; --j) {
         float2 Cq[2];
@@ -446,6 +447,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         for (int ii = 1; ii >= 0; --ii) {
           const int i = 2 * j + ii;
           const float2 e = mul2(dy[i], Cq[ii]);  // e_t = dy_t C_t
+          ev[i] = e;
           Gr = fmaf(i == kHalf - 1 ? 0.f : ab[i + 1].x, Gr, e.y);
           Gr = fmaf(ab[i].y, Gr, e.x);
         }
@@ -470,13 +472,12 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       float2 dAl = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = kHalf / 2 - 1; j >= 0; --j) {
-        float2 Bq[2], Cq[2], dbp[2];
+        float2 Bq[2], dbp[2];
         lds_quad(bB, lane, j, Bq);
-        lds_quad(bC, lane, j, Cq);
 #pragma unroll
         for (int ii = 1; ii >= 0; --ii) {
           const int i = 2 * j + ii;
-          const float2 e = mul2(dy[i], Cq[ii]);
+          const float2 e = ev[i];
           float2 gv;
           gv.y = g = fmaf(i == kHalf - 1 ? an_last : ab[i + 1].x, g, e.y);
           gv.x = g = fmaf(ab[i].y, g, e.x);
