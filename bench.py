@@ -41,6 +41,10 @@ CONFIGS = {
     "c2": dict(workload="configs[2]: fused selective scan fwd+bwd, Mamba-2.8B layer shape, "
                         "bf16 I/O, right padding",
                batch=16, dim=5120, length=4096, dstate=16, dtype="bf16", padded=True),
+    "c4": dict(workload="configs[4] single-sequence variant: one Mamba-2.8B layer's scan, "
+                        "B=1, L=131072, d_inner 5120 sharded over the GPUs (channel sharding)",
+               batch=1, dim=5120, length=131072, dstate=16, dtype="bf16", padded=False,
+               shard="channels"),
 }
 
 
@@ -111,8 +115,9 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- GPU arm
-def _algorithmic(cfg, esize):
-    b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+def _algorithmic(cfg, esize, d=None):
+    b, L, n = cfg["batch"], cfg["length"], cfg["dstate"]
+    d = cfg["dim"] if d is None else d
     elems = b * d * L
     bnl = b * n * L
     nch = math.ceil(L / 512)
@@ -134,7 +139,8 @@ def run_gpu(args, cfg):
     import torch.distributed as dist
 
     from mamba import selective_scan_cuda as ssc
-    from mamba.distributed import allreduce_param_grads, flat_param_grads
+    from mamba.distributed import (allreduce_bc_grads, allreduce_param_grads, channel_shard,
+                                   flat_param_grads)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -145,6 +151,11 @@ def run_gpu(args, cfg):
         dist.init_process_group("nccl", device_id=dev)
 
     b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+    chan = cfg.get("shard") == "channels"
+    d_total = d
+    if chan:  # this rank's block of channels; B and C are shared
+        sl = channel_shard(d, rank, world)
+        d = sl.stop - sl.start
     io = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
     esize = 2 if io == torch.bfloat16 else 4
     g = torch.Generator(device=dev)
@@ -185,10 +196,16 @@ def run_gpu(args, cfg):
                                 dout, None, du, ddl, dA, dB, dC, dDp, dz, dbias, None, ws,
                                 out_pre=pre)
 
+    def exchange():
+        if chan:
+            allreduce_bc_grads(dB, dC)  # dB, dC sum over every channel
+        else:
+            allreduce_param_grads(params)  # dA, dD, ddelta_bias sum over sequences
+
     def step():
         fwd()
         bwd()
-        allreduce_param_grads(params)
+        exchange()
 
     for _ in range(max(args.warmup, 0)):
         step()
@@ -209,7 +226,7 @@ def run_gpu(args, cfg):
             ev[i][1].record(stream)
             bwd()
             ev[i][2].record(stream)
-            allreduce_param_grads(params)
+            exchange()
         t_end.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -224,7 +241,7 @@ def run_gpu(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
 
-    elems, fwd_bytes, bwd_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize)
+    elems, fwd_bytes, bwd_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize, d)
     # padded steps are skipped by the kernels: the rooflines count
     # the valid steps only, the headline value counts every B*D*L position
     valid = 1.0
@@ -232,10 +249,11 @@ def run_gpu(args, cfg):
         valid = float(seq_lens.sum().item()) / (b * L)
     fwd_bytes, bwd_bytes = fwd_bytes * valid, bwd_bytes * valid
     ms_per_step = total_ms / args.steps
-    value = elems * world / (ms_per_step * 1e-3) / 1e9
+    total_elems = b * d_total * L if chan else elems * world
+    value = total_elems / (ms_per_step * 1e-3) / 1e9
 
     # ---- e2e through the public API with host buffers
-    e2e = run_e2e(args, cfg, dev, io, rank, world) if args.e2e else None
+    e2e = run_e2e(args, cfg, dev, io, rank, world) if args.e2e and not chan else None
 
     if rank != 0:
         if world > 1:
@@ -257,11 +275,12 @@ def run_gpu(args, cfg):
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if chan else "weak", "vs_baseline": None,
         "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1)/U(-4,-2) inputs of the config)",
-        "config": {"workload": cfg["workload"], "batch_per_gpu": b, "dim": d, "length": L,
+        "config": {"workload": cfg["workload"], "batch_per_gpu": b, "dim": d_total, "dim_per_gpu": d, "length": L,
                    "dstate": n, "global_batch": b * world,
-                   "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"channel-sharded over {world} GPUs ({d} channels each)" if chan
+                                   else f"batch-sharded dp{world}") if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (u, delta, z, dy: "
                          f"{elems * esize * 4 / 1e6:.0f} MB per step)",
                    "valid_fraction": round(valid, 4)},

@@ -1,11 +1,20 @@
-"""Data-parallel plumbing for the selective scan (one process per GPU).
+"""Multi-GPU plumbing for the selective scan (one process per GPU).
 
-The scan's work partitions by sequence: each rank scans its own slice of the
-batch with no exchange in the data path. The only collective is the sum over
-ranks of the parameter gradients dA (D, N), dD (D) and ddelta_bias (D),
-done as one all-reduce of a flat buffer (NCCL over NVLink on the GPU box,
-gloo in the CPU tests). The reference has no distributed code; its
-parameters would be reduced by XLA's psum under shard_map.
+Two partitions of the scan's work:
+
+* batch sharding: each rank scans its own sequences with no exchange in the
+  data path; the only collective is the sum over ranks of the parameter
+  gradients dA (D, N), dD (D) and ddelta_bias (D), one all-reduce of a flat
+  buffer;
+* channel sharding, for single long sequences: each rank owns a contiguous
+  block of the d_inner channels (every channel's recurrence is independent),
+  and B, C are shared; dA, dD and ddelta_bias are per channel and need no
+  collective, but dB and dC are sums over all channels, so they are
+  all-reduced.
+
+The collectives are NCCL over NVLink on the GPU box and gloo in the CPU
+tests. The reference has no distributed code; under JAX these would be
+XLA psums inside shard_map.
 """
 from __future__ import annotations
 
@@ -20,6 +29,19 @@ def batch_shard(global_batch: int, rank: int, world: int) -> slice:
     base, extra = divmod(global_batch, world)
     start = rank * base + min(rank, extra)
     return slice(start, start + base + (1 if rank < extra else 0))
+
+
+def channel_shard(dim: int, rank: int, world: int) -> slice:
+    """Contiguous block of channels owned by `rank` (same split as batch_shard)."""
+    return batch_shard(dim, rank, world)
+
+
+def allreduce_bc_grads(dB: torch.Tensor, dC: torch.Tensor, group=None):
+    """Sum dB and dC over the channel shards, in place (one all-reduce each)."""
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    dist.all_reduce(dB, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(dC, op=dist.ReduceOp.SUM, group=group)
 
 
 def flat_param_grads(dim: int, dstate: int, device=None, dtype=torch.float32):

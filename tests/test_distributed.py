@@ -74,3 +74,52 @@ def test_two_rank_gradient_allreduce_matches_full_batch():
     np.testing.assert_allclose(dA, full["dA"], rtol=1e-12, atol=1e-12)
     np.testing.assert_allclose(dD, full["dD"], rtol=1e-12, atol=1e-12)
     np.testing.assert_allclose(dbias, full["ddelta_bias"], rtol=1e-12, atol=1e-12)
+
+
+def _rank_channels(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mamba.distributed import allreduce_bc_grads, channel_shard
+        from oracle import selective_scan_oracle as orc
+
+        x = orc.make_inputs(1, 10, 60, 8, seed=4, initial_state=True)
+        sl = channel_shard(10, rank, world)
+        ch = {"u", "delta", "z", "dout"}
+        sub = {k: (v[:, sl] if k in ch else v) for k, v in x.items()}
+        g = orc.fused_backward(sub["u"], sub["delta"], x["A"][sl], x["B"], x["C"], x["D"][sl],
+                               sub["z"], x["delta_bias"][sl], True, x["initial_state"][:, sl],
+                               True, None, dout=sub["dout"])
+        dB = torch.from_numpy(g["dB"].copy())
+        dC = torch.from_numpy(g["dC"].copy())
+        allreduce_bc_grads(dB, dC)
+        q.put((rank, dB.numpy(), dC.numpy(), g["dA"], g["du"]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_channel_sharding_matches_full_sequence():
+    from mamba.distributed import channel_shard
+    from oracle import selective_scan_oracle as orc
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_channels, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r[0], r[1:]) for r in (q.get(timeout=120), q.get(timeout=120)))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    x = orc.make_inputs(1, 10, 60, 8, seed=4, initial_state=True)
+    full = orc.fused_backward(x["u"], x["delta"], x["A"], x["B"], x["C"], x["D"], x["z"],
+                              x["delta_bias"], True, x["initial_state"], True, None,
+                              dout=x["dout"])
+    for r in (0, 1):
+        dB, dC, dA, du = res[r]
+        np.testing.assert_allclose(dB, full["dB"], rtol=1e-12, atol=1e-12)
+        np.testing.assert_allclose(dC, full["dC"], rtol=1e-12, atol=1e-12)
+        sl = channel_shard(10, r, 2)
+        np.testing.assert_allclose(dA, full["dA"][sl], rtol=1e-12, atol=1e-12)
+        np.testing.assert_allclose(du, full["du"][:, sl], rtol=1e-12, atol=1e-12)
