@@ -62,7 +62,7 @@ struct BwdShared {
   alignas(1024) T arrD[kBwdWarps][32][kItems];
   // per-warp dB/dC rows of the current state, in tile_slot order. Before the
   // state loop the same bytes hold the chunk's z, dout and pre-gate runs
-  // (zone offsets 0, kArr and 16 KiB); dz is staged in the pre-gate slot,
+  // (zone offsets 0, kArr and half of wrow); dz is staged in the pre-gate slot,
   // which lies in the half used from the second state on.
   alignas(1024) float4 wrow[2][kBwdWarps][2][kChunk / 4];
   float gcarry[kBwdWarps][NS];
@@ -73,11 +73,13 @@ struct BwdShared {
   static constexpr int kArr = kBwdWarps * 32 * kItems;  // elements per chunk array
   __device__ T (*zone(int k))[32][kItems] {
     unsigned char* base = reinterpret_cast<unsigned char*>(&wrow[0][0][0][0]);
-    const size_t off = k == 0 ? 0 : k == 1 ? kArr * sizeof(T) : 16384;
+    const size_t off = k == 0 ? 0 : k == 1 ? kArr * sizeof(T) : sizeof(wrow) / 2;
     return reinterpret_cast<T(*)[32][kItems]>(base + off);
   }
 };
-static_assert(3 * 4 * 32 * kItems * 4 <= 2 * 4 * 2 * (kChunk / 4) * 16, "zone fits wrow");
+// z and dout fit the first half of wrow, the pre-gate runs the second half
+static_assert(2 * kBwdWarps * 32 * kItems * 4 <= kBwdWarps * 2 * (kChunk / 4) * 16,
+              "zone fits wrow");
 
 // Staged B/C rows hold 32 lane runs of kItems steps. fp32 runs are 64 bytes
 // with the TMA's 64-byte swizzle (16-byte chunk j of run r sits at chunk
