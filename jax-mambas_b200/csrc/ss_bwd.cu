@@ -219,6 +219,18 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
 
   float dD_acc = 0.f, dbias_acc = 0.f;
 
+  // dB/dC flush: each thread owns the same kFlushPerThread float4 groups of
+  // every state's rows; their shared-memory slots are fixed.
+  constexpr int kFlushPerThread = 2 * (kChunk / 4) / (kBwdWarps * 32);
+  static_assert(kFlushPerThread * kBwdWarps * 32 == 2 * (kChunk / 4), "flush split");
+  int flush_slot[kFlushPerThread];
+#pragma unroll
+  for (int k = 0; k < kFlushPerThread; ++k)
+    flush_slot[k] = tile_slot((threadIdx.x + k * kBwdWarps * 32) % (kChunk / 4));
+  // 16-byte atomics need 16-byte aligned accumulator rows (L % 4 == 0)
+  const bool acc_aligned = (L & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.dB_acc) |
+                                              reinterpret_cast<uintptr_t>(p.dC_acc)) & 15) == 0;
+
   for (int c = p.n_chunks - 1; c >= 0; --c) {
     const int t0 = c * kChunk;
     const int tl = t0 + lane * kItems;
@@ -524,22 +536,27 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       // ---- add the warps' dB/dC rows of this state into the fp32 accumulators
       {
         const size_t base = (static_cast<size_t>(b) * NS + n) * L;
-        for (int q = threadIdx.x; q < 2 * (kChunk / 4); q += blockDim.x) {
+        const bool whole = t0 + kChunk <= len;  // CTA-uniform
+#pragma unroll
+        for (int k = 0; k < kFlushPerThread; ++k) {
+          const int q = threadIdx.x + k * kBwdWarps * 32;
           const int which = q / (kChunk / 4);  // 0: dB, 1: dC
           const int qq = q % (kChunk / 4);
-          const int slot = tile_slot(qq);
-          float4 v = sh.wrow[sb][0][which][slot];
+          const float4* src = &sh.wrow[sb][0][which][flush_slot[k]];
+          float4 v0 = src[0];
+          float2 lo = make_float2(v0.x, v0.y), hi = make_float2(v0.z, v0.w);
 #pragma unroll
           for (int w = 1; w < kBwdWarps; ++w) {
-            const float4 x = sh.wrow[sb][w][which][slot];
-            v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+            const float4 x = src[w * 2 * (kChunk / 4)];
+            lo = add2(lo, make_float2(x.x, x.y));
+            hi = add2(hi, make_float2(x.z, x.w));
           }
+          const float4 v = make_float4(lo.x, lo.y, hi.x, hi.y);
+          float* gp = (which ? p.dC_acc : p.dB_acc) + base + t0 + qq * 4;
           const int t = t0 + qq * 4;
-          if (t >= len) continue;
-          float* gp = (which ? p.dC_acc : p.dB_acc) + base + t;
-          if (t + 4 <= len && ((reinterpret_cast<uintptr_t>(gp) & 15) == 0)) {
+          if (whole && acc_aligned) {
             atomicAdd(reinterpret_cast<float4*>(gp), v);
-          } else {
+          } else if (t < len) {
             const float e4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
