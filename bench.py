@@ -390,6 +390,71 @@ def run_e2e(args, cfg, dev, io, rank, world):
             "api": "mamba.selective_scan_cuda.selective_scan_fn + autograd backward"}
 
 
+# ---------------------------------------------------------------- decode step
+def run_step_bench(args):
+    """--config step: one recurrent decode step (S6.step) of a Mamba-2.8B layer
+    for a batch of 32 sequences: bf16 token inputs, fp32 state updated in
+    place. HBM-bound; reported as channel-updates/s and GB/s of state +
+    token traffic against the measured copy bandwidth."""
+    import torch
+
+    from mamba.selective_scan_cuda import fused_step_into
+
+    dev = torch.device("cuda", 0)
+    b, d, n = 32, 5120, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    bf = torch.bfloat16
+    # several independent states, cycled, so that state traffic exceeds L2
+    copies = 16
+    states = [torch.randn(b, d, n, generator=g, device=dev) for _ in range(copies)]
+    u, dl, z = (torch.randn(b, d, generator=g, device=dev).to(bf) for _ in range(3))
+    Bm, Cm = (torch.randn(b, n, generator=g, device=dev).to(bf) for _ in range(2))
+    A = (-torch.arange(1, n + 1, device=dev, dtype=torch.float32)).expand(d, n).contiguous()
+    Dp = torch.randn(d, generator=g, device=dev)
+    bias = torch.rand(d, generator=g, device=dev) * 2 - 4
+    out = torch.empty_like(u)
+    steps = max(args.steps, 64) // copies * copies
+
+    def launch_all():
+        for i in range(steps):
+            fused_step_into(states[i % copies], u, dl, A, Bm, Cm, Dp, z, bias, True, out)
+
+    # decode is launch-bound from Python: capture the steps in a CUDA graph
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        launch_all()  # warm-up outside the graph
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        launch_all()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    graph.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / steps
+    nbytes = b * d * n * 4 * 2 + b * d * 2 * 4 + 2 * b * n * 2 + d * n * 4 + 2 * d * 4
+    hbm, _, src = _peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "selective-state-update (decode step) channel updates/s", "unit": "Gupd/s",
+        "value": round(b * d / (ms * 1e-3) / 1e9, 3), "ms_per_step": round(ms, 5),
+        "steps": steps, "higher_is_better": True, "dtype": "bf16 I/O, fp32 state",
+        "data": "synthetic", "n_gpus": 1,
+        "config": {"workload": "one decode token of a Mamba-2.8B layer (S6.step), "
+                               "steps replayed from a CUDA graph", "batch": b,
+                   "dim": d, "dstate": n, "l2": f"{copies} states cycled ({copies * b * d * n * 4 / 1e6:.0f} MB)"},
+        "roofline": {"bound": "hbm", "kernel": "ss_step_kernel", "achieved": round(gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                     "peak_source": src, "algorithmic_bytes_per_launch": nbytes},
+        "gpu_launches": steps}), flush=True)
+
+
 # ---------------------------------------------------------------- CPU arm
 def _cpu_sample_shape(cfg, seconds_target):
     # a bounded sample: full length and state size, a slice of the channels
@@ -472,7 +537,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["step"], default="c1")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -481,6 +546,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.config == "step":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the decode-step leg has no "
+                              "CPU reference arm; see --config c1"}))
+        else:
+            run_step_bench(args)
+        return
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         run_reference(args, cfg)

@@ -139,6 +139,17 @@ mss_status mamba_ss_fused_bwd(
     void* dz, float* ddelta_bias, float* dinitial_state, void* workspace,
     size_t workspace_bytes);
 
+/* One recurrent decode step: the state update of S6.step / Mamba.step
+ * (mamba/mamba1.py:200-214; pure JAX in the reference, no FFI counterpart).
+ * For one new token per sequence: u, delta, z, out are (batch, dim), B, C
+ * (batch, dstate) in io_dtype; state (batch, dim, dstate) fp32 is updated in
+ * place (16-byte aligned); A, D, delta_bias as in mamba_ss_fused_fwd. */
+mss_status mamba_ss_fused_step(void* stream, int32_t io_dtype, int32_t discretization,
+                               int32_t batch, int32_t dim, int32_t dstate, float* state,
+                               const void* u, const void* delta, const float* A,
+                               const void* B, const void* C, const float* D, const void* z,
+                               const float* delta_bias, int32_t delta_softplus, void* out);
+
 /* ---------------------------------------------------------------------------
  * Allocation-free backward. No counterpart in the reference.
  *

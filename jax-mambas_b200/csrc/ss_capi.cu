@@ -218,6 +218,39 @@ mss_status mamba_ss_fused_bwd(
   return MSS_OK;
 }
 
+mss_status mamba_ss_fused_step(void* stream, int32_t io_dtype, int32_t discretization,
+                               int32_t batch, int32_t dim, int32_t dstate, float* state,
+                               const void* u, const void* delta, const float* A,
+                               const void* B, const void* C, const float* D, const void* z,
+                               const float* delta_bias, int32_t delta_softplus, void* out) {
+  mss_status st = check_dims("mamba_ss_fused_step", io_dtype, discretization, batch, 1, dim,
+                             dstate);
+  if (st != MSS_OK) return st;
+  if (!state || !u || !delta || !A || !B || !C || !out)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_fused_step: state, u, delta, A, B, C and out must be non-null");
+  if (reinterpret_cast<uintptr_t>(state) & 15)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_step: state must be 16-byte aligned");
+  mss::StepParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.delta_softplus = delta_softplus ? 1 : 0;
+  p.state = state;
+  p.u = u;
+  p.delta = delta;
+  p.z = z;
+  p.B = B;
+  p.C = C;
+  p.A = A;
+  p.D = D;
+  p.delta_bias = delta_bias;
+  p.out = out;
+  cudaError_t e = mss::launch_step(p, dstate, io_dtype, discretization,
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching selective scan step", e);
+  return MSS_OK;
+}
+
 mss_status mamba_ss_fwd(void* stream, int32_t discretization, int32_t batch,
                         int32_t length, int32_t dim, int32_t dstate,
                         const float* A, const float* deltas, const float* B,

@@ -75,6 +75,21 @@ struct BwdParams {
   float* dh0;
 };
 
+struct StepParams {
+  int batch, dim;
+  int delta_softplus;
+  float* state;  // (batch, dim, dstate) fp32, updated in place
+  const void* u;
+  const void* delta;
+  const void* z;
+  const void* B;
+  const void* C;
+  const float* A;
+  const float* D;
+  const float* delta_bias;
+  void* out;
+};
+
 // ---------------------------------------------------------------- typed I/O
 template <typename T>
 struct Elem;

@@ -21,6 +21,9 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream);
 
+cudaError_t launch_step(const StepParams& p, int dstate, int io_dtype, int zoh,
+                        cudaStream_t stream);
+
 // Records `msg` as this host thread's mamba_ss_last_error() and returns code.
 mss_status set_error(mss_status code, const std::string& msg);
 

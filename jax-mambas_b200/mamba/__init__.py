@@ -4,4 +4,5 @@ from .selective_scan_cuda import (  # noqa: F401
     selective_scan,
     selective_scan_fn,
     selective_scan_reference,
+    selective_state_update,
 )

@@ -56,6 +56,12 @@ SIGNATURES = {
         + [_c_void_p] * 16  # initial_state seq_lens chunk_states out_pre dout dlast du ddelta dA dB dC dD dz dbias dinit workspace
         + [ctypes.c_size_t],
     ),
+    "mamba_ss_fused_step": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i32, _i32]
+        + [_c_void_p] * 8  # state u delta A B C D z
+        + [_c_void_p, _i32, _c_void_p],  # delta_bias delta_softplus out
+    ),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,

@@ -302,6 +302,56 @@ def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None,
 
 
 # --------------------------------------------------------------------------
+# Recurrent decode step (S6.step / Mamba.step, mamba/mamba1.py:200-214)
+# --------------------------------------------------------------------------
+def selective_state_update(state, u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                           delta_softplus=False, *, use_euler_barB_approx=True):
+    """One decode step for one new token per sequence on the sm_100a kernel.
+
+    state (B, D, N) fp32 is updated in place; u, delta, z are (B, D) and B, C
+    (B, N) in fp32 or bf16; returns out (B, D) = (C . h + D u) * silu(z).
+    """
+    if state.ndim != 3 or state.dtype != torch.float32:
+        raise ValueError("state must be a float32 tensor of shape (B, D, N)")
+    batch, dim, n = state.shape
+    if n not in _VALID_N:
+        raise ValueError("N must be one of 1, 2, 4, 8, or 16")
+    io = u.dtype
+    for name, t, shape in (("u", u, (batch, dim)), ("delta", delta, (batch, dim)),
+                           ("B", B, (batch, n)), ("C", C, (batch, n)), ("z", z, (batch, dim))):
+        if t is None:
+            continue
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {shape}, got {tuple(t.shape)}")
+        if t.dtype != io:
+            raise TypeError(f"{name} must have dtype {io}")
+    for t in (state, u, delta, A, B, C, D, z, delta_bias):
+        if t is not None and not t.is_cuda:
+            raise ValueError("selective_state_update needs CUDA tensors")
+    if not state.is_contiguous():
+        raise ValueError("state must be contiguous (it is updated in place)")
+    c = lambda t: None if t is None else t.contiguous()
+    u, delta, A, B, C, D, z, delta_bias = map(c, (u, delta, A, B, C, D, z, delta_bias))
+    out = torch.empty_like(u)
+    fused_step_into(state, u, delta, A, B, C, D, z, delta_bias, delta_softplus, out,
+                    zoh=not use_euler_barB_approx)
+    return out
+
+
+def fused_step_into(state, u, delta, A, B, C, D, z, delta_bias, delta_softplus, out,
+                    zoh=False):
+    """Launch one decode step on the current stream into a given `out`
+    (contiguous CUDA tensors, no checks beyond the C ABI's)."""
+    lib = _lib()
+    batch, dim, n = state.shape
+    st = lib.mamba_ss_fused_step(
+        _stream(u.device), _io_dtype(u), int(zoh), batch, dim, n,
+        _ptr(state), _ptr(u), _ptr(delta), _ptr(A), _ptr(B), _ptr(C), _ptr(D), _ptr(z),
+        _ptr(delta_bias), int(bool(delta_softplus)), _ptr(out))
+    _native.check(lib, st)
+
+
+# --------------------------------------------------------------------------
 # Reference contract (reference :217-308)
 # --------------------------------------------------------------------------
 class _SelectiveScanCuda(torch.autograd.Function):

@@ -247,6 +247,30 @@ def fused_backward(u, delta, A, B, C, D=None, z=None, delta_bias=None,
     }
 
 
+def fused_step(state, u, delta, A, B, C, D=None, z=None, delta_bias=None,
+               delta_softplus=False, use_euler_barB_approx=True, dtype=np.float64):
+    """One decode step, restating S6.step (mamba/mamba1.py:200-214) plus the
+    fused gate: returns (out (B, D), new_state (B, D, N))."""
+    f = lambda x: None if x is None else np.asarray(x, dtype=dtype)
+    state, u, delta, A, B, C, D, z, delta_bias = map(
+        f, (state, u, delta, A, B, C, D, z, delta_bias))
+    pre = delta + (delta_bias[None, :] if delta_bias is not None else 0.0)
+    dl = _softplus(pre) if delta_softplus else pre
+    dA = dl[:, :, None] * A[None]
+    a = np.exp(dA)
+    if use_euler_barB_approx:
+        bbar = dl[:, :, None] * B[:, None, :]
+    else:
+        bbar = np.expm1(dA) / A[None] * B[:, None, :]
+    h = a * state + bbar * u[:, :, None]
+    y = np.einsum("bn,bdn->bd", C, h)
+    if D is not None:
+        y = y + D[None, :] * u
+    if z is not None:
+        y = y * z * _sigmoid(z)
+    return y, h
+
+
 # --------------------------------------------------------------------------
 # Seeded inputs with the distributions of the benchmark configurations.
 # --------------------------------------------------------------------------
