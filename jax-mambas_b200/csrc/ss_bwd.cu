@@ -24,6 +24,8 @@
 // and adds the result to the fp32 accumulators in global memory with 16-byte
 // atomics.
 #include <algorithm>
+#include <cstddef>
+#include <cstdlib>
 #include <cstring>
 
 #include "ss_common.cuh"
@@ -188,7 +190,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
   const bool use_tma = p.tma_ok != 0;
   // chunks at or past `len` are padding only and skipped; the TMA pipeline
   // walks (chunk, state) for the others, chunks in reverse
-  const int c_first = len > 0 ? min(p.n_chunks - 1, (len - 1) / kChunk) : -1;
+  const int n_big = (L + kChunk - 1) / kChunk;  // chunks of kChunk steps
+  const int c_first = len > 0 ? min(n_big - 1, (len - 1) / kChunk) : -1;
   auto issue = [&](int c, int n, int seq) {  // one thread
     uint64_t* bar = &sh.bar[seq & 1];
     mbar_arrive_expect_tx(bar, 2u * 32u * kItems * sizeof(T));
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
   const bool acc_aligned = (L & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.dB_acc) |
                                               reinterpret_cast<uintptr_t>(p.dC_acc)) & 15) == 0;
 
-  for (int c = p.n_chunks - 1; c >= 0; --c) {
+  for (int c = n_big - 1; c >= 0; --c) {
     const int t0 = c * kChunk;
     const int tl = t0 + lane * kItems;
 
@@ -345,7 +348,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         if (c == 0)
           hsv = p.h0 ? __ldg(p.h0 + row * NS + lane) : 0.f;
         else
-          hsv = p.chunk_states[(row * p.n_chunks + c - 1) * NS + lane];
+          hsv = p.chunk_states[(row * p.n_chunks + c * (kChunk / kCkpt) - 1) * NS + lane];
       }
       sh.hsw[warp][lane] = hsv;
     }
@@ -632,6 +635,626 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
   }
 }
 
+// ============================================================================
+// Tile backward (the default): sequential in time inside each lane.
+//
+// A lane owns kS states of one channel, kLPC = NS / kS lanes a channel, and a
+// one-warp CTA kCh = 32 / kLPC channels of one batch (the forward's
+// decomposition). The forward saves the state at the end of every kBT-step
+// tile, so tiles are independent given their entering state. The CTA walks
+// the tiles in reverse; per tile
+//   0. TMA stages delta, u, dout, z, pre-gate ([kCh channels x kBT steps])
+//      and B, C ([N x kBT]) with the 128-byte (fp32) / 64-byte (bf16)
+//      swizzle; the next tile's copies fly while this one computes;
+//   1. transform: delta_eff = softplus(delta + bias) and dy = dout silu(z)
+//      become fp32 work rows (for fp32 I/O in place of delta and dout), and
+//      dz = dout pre silu'(z) is written in place of z;
+//   2. forward pass over the tile from its saved state, keeping the state at
+//      the start of each kGrp-step group in registers;
+//   3. groups in reverse: recompute a_t, h_t over the group, run the adjoint
+//      g_t = dy_t C_t + a_{t+1} g_{t+1} per state, and form per step
+//      sum_n g B and sum_n g A a h_{t-1} (summed over the channel's lanes,
+//      then du, ddelta written in place of u and delta), per lane dA, and
+//      dB = g delta u, dC = dy h per (channel, state) into a shared tile that
+//      the warp sums over channels and adds to the fp32 accumulators with
+//      16-byte atomics;
+//   4. the tile's du, ddelta and dz leave by TMA bulk stores.
+// Shared memory is kept under 20 KB per CTA (fp32, N = 16) so that a
+// Mamba-130M layer's CTAs are all resident at once (11 per SM).
+// ============================================================================
+constexpr int kBT = kCkpt;      // steps per tile (one saved carry per tile)
+constexpr int kGrp = 4;         // steps per group
+constexpr int kNG = kBT / kGrp;  // groups per tile
+
+template <int NS>
+struct TileCfg {
+  static constexpr int kS = NS < 4 ? NS : 4;  // states per lane
+  static constexpr int kLPC = NS / kS;        // lanes per channel
+  static constexpr int kCh = 32 / kLPC;       // channels per CTA (one warp)
+  // column swizzle of the [channel][state] dB/dC tile: the 32 lanes' float4
+  // writes of one state index, and the flush's row reads, avoid bank conflicts
+  static __device__ __forceinline__ int part_swz(int c) {
+    return NS == 16 ? (c & 1) << 2 : NS == 8 ? (c & 3) << 1 : NS == 4 ? (c & 3)
+                                             : NS == 2 ? (c >> 2) & 1 : 0;
+  }
+};
+
+struct TileMaps {
+  CUtensorMap d, u, y, z, p, b, c;  // loads: [rows][L], boxes [box rows][kBT]
+  CUtensorMap du, dd, dz;           // stores
+};
+
+template <int NS, typename T>
+struct TileShared {
+  static constexpr int kCh = TileCfg<NS>::kCh;
+  static constexpr int kNSP = NS < 8 ? 8 : NS;  // whole swizzle atoms
+  static constexpr bool kInPlace = sizeof(T) == 4;  // fp32 work rows live in rawD / rawY
+  alignas(1024) T rawD[2][kCh][kBT];  // delta in; (fp32: delta_eff;) ddelta out
+  alignas(1024) T rawU[2][kCh][kBT];  // u in, du out
+  alignas(1024) T rawY[2][kCh][kBT];  // dout in; (fp32: dy)
+  alignas(1024) T rawZ[2][kCh][kBT];  // z in, dz out
+  alignas(1024) T rawB[2][kNSP][kBT];
+  alignas(1024) T rawC[2][kNSP][kBT];
+  alignas(1024) T rawP[kCh][kBT];     // pre-gate output (read by the transform only)
+  // bf16 I/O: fp32 work rows delta_eff and dy, swizzled like fp32 staging
+  alignas(16) float wD[kInPlace ? 1 : kCh][kBT];
+  alignas(16) float wY[kInPlace ? 1 : kCh][kBT];
+  float4 part[kCh][NS];  // one group's dB or dC per (channel, swizzled state)
+  uint64_t bar[2];
+  uint64_t barP;
+};
+
+// Element (r, t) of a staged [rows][kBT] tile: fp32 rows are 128 bytes under
+// the 128-byte swizzle (16-byte chunk j of row r at j ^ (r & 7)), bf16 rows
+// 64 bytes under the 64-byte swizzle (chunk j at j ^ ((r >> 1) & 3)).
+__device__ __forceinline__ int sw_idx(const float*, int r, int t) {
+  return r * kBT + ((((t >> 2) ^ (r & 7)) << 2) | (t & 3));
+}
+__device__ __forceinline__ int sw_idx(const __nv_bfloat16*, int r, int t) {
+  return r * kBT + ((((t >> 3) ^ ((r >> 1) & 3)) << 3) | (t & 7));
+}
+
+// Steps t .. t+3 (t a multiple of 4) of row r as fp32.
+__device__ __forceinline__ float4 ld4s(const float* tile, int r, int t) {
+  return *reinterpret_cast<const float4*>(tile + sw_idx(tile, r, t));
+}
+__device__ __forceinline__ float4 ld4s(const __nv_bfloat16* tile, int r, int t) {
+  const uint2 w = *reinterpret_cast<const uint2*>(tile + sw_idx(tile, r, t));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st4s(float* tile, int r, int t, float4 v) {
+  *reinterpret_cast<float4*>(tile + sw_idx(tile, r, t)) = v;
+}
+__device__ __forceinline__ void st4s(__nv_bfloat16* tile, int r, int t, float4 v) {
+  uint2 w;
+  *reinterpret_cast<__nv_bfloat162*>(&w.x) = __floats2bfloat162_rn(v.x, v.y);
+  *reinterpret_cast<__nv_bfloat162*>(&w.y) = __floats2bfloat162_rn(v.z, v.w);
+  *reinterpret_cast<uint2*>(tile + sw_idx(tile, r, t)) = w;
+}
+template <typename T>
+__device__ __forceinline__ float ld1s(const T* tile, int r, int t) {
+  return to_f32(tile[sw_idx(tile, r, t)]);
+}
+template <typename T>
+__device__ __forceinline__ void st1s(T* tile, int r, int t, float v) {
+  tile[sw_idx(tile, r, t)] = static_cast<T>(v);
+}
+
+// Plain-load staging of a [box_rows][kBT] tile in the TMA's swizzled layout:
+// rows at or past n_valid and steps at or past L read as zero (one warp).
+template <typename T>
+__device__ void stage_tile_plain(T* tile, const T* base, size_t row0, int n_valid, int box_rows,
+                                 int L, int t0, int lane) {
+  for (int i = lane; i < box_rows * kBT; i += 32) {
+    const int r = i / kBT, t = i % kBT;
+    T v = static_cast<T>(0.f);
+    if (r < n_valid && t0 + t < L) v = base[(row0 + r) * static_cast<size_t>(L) + t0 + t];
+    tile[sw_idx(tile, r, t)] = v;
+  }
+}
+
+// Plain stores of a staged tile's rows below n_valid, steps below L (one warp).
+template <typename T>
+__device__ void unstage_tile_plain(T* base, const T* tile, size_t row0, int n_valid, int L,
+                                   int t0, int lane) {
+  for (int i = lane; i < n_valid * kBT; i += 32) {
+    const int r = i / kBT, t = i % kBT;
+    if (t0 + t < L) base[(row0 + r) * static_cast<size_t>(L) + t0 + t] = tile[sw_idx(tile, r, t)];
+  }
+}
+
+// Zeroes steps [from, L) of n rows (one warp); 16-byte stores when `vec`.
+template <typename T>
+__device__ void zero_rows(T* base, size_t row0, int n, int L, int from, bool vec, int lane) {
+  if (from >= L) return;
+  constexpr int kPer = 16 / sizeof(T);
+  for (int r = 0; r < n; ++r) {
+    T* rowp = base + (row0 + r) * static_cast<size_t>(L);
+    if (vec) {
+      for (int t = from + lane * kPer; t < L; t += 32 * kPer)
+        *reinterpret_cast<uint4*>(rowp + t) = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      for (int t = from + lane; t < L; t += 32) rowp[t] = static_cast<T>(0.f);
+    }
+  }
+}
+
+// Sums one group's [channel][state] tile over the channels and adds state
+// row n's four steps into acc_b[n * L + t] (t = the group's first step).
+// Lane o + NS*h sums channels h*kS .. h*kS + kS - 1 of state o, then the
+// 32/NS lanes of a state combine with xor-shuffles.
+template <int NS>
+__device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_b, int L, int t,
+                                           int len, bool whole, int lane) {
+  using Cfg = TileCfg<NS>;
+  const int o = lane % NS, h = lane / NS;
+  float2 lo = make_float2(0.f, 0.f), hi = lo;
+#pragma unroll
+  for (int i = 0; i < Cfg::kS; ++i) {
+    const int c = h * Cfg::kS + i;
+    const float4 v = part[c][o ^ Cfg::part_swz(c)];
+    lo = add2(lo, make_float2(v.x, v.y));
+    hi = add2(hi, make_float2(v.z, v.w));
+  }
+#pragma unroll
+  for (int m = NS; m < 32; m <<= 1) {
+    lo.x += __shfl_xor_sync(0xffffffffu, lo.x, m);
+    lo.y += __shfl_xor_sync(0xffffffffu, lo.y, m);
+    hi.x += __shfl_xor_sync(0xffffffffu, hi.x, m);
+    hi.y += __shfl_xor_sync(0xffffffffu, hi.y, m);
+  }
+  if (h == 0) {
+    float* gp = acc_b + static_cast<size_t>(o) * L + t;
+    if (whole) {
+      atomicAdd(reinterpret_cast<float4*>(gp), make_float4(lo.x, lo.y, hi.x, hi.y));
+    } else {
+      const float e4[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (t + e < len) atomicAdd(gp + e, e4[e]);
+    }
+  }
+}
+
+template <int NS, typename T, bool kZOH>
+__global__ void __launch_bounds__(32)
+    ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
+  using Cfg = TileCfg<NS>;
+  using Sh = TileShared<NS, T>;
+  constexpr int kS = Cfg::kS;
+  constexpr int kLPC = Cfg::kLPC;
+  constexpr int kCh = Cfg::kCh;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
+
+  const int lane = threadIdx.x;
+  const int b = blockIdx.y;
+  const int d0 = blockIdx.x * kCh;
+  const int L = p.seqlen;
+  const int n_ch = min(kCh, p.dim - d0);
+  const int c = lane / kLPC;  // channel slot
+  const int q = lane % kLPC;  // lane q owns states q, q + kLPC, ...
+  const bool act = c < n_ch;
+  const int d = d0 + (act ? c : 0);
+  const size_t row = static_cast<size_t>(b) * p.dim + d;
+  const size_t row0 = static_cast<size_t>(b) * p.dim + d0;  // first row of the CTA
+
+  int len = L;
+  if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
+  const int k_last = len > 0 ? (len - 1) / kBT : -1;  // last tile with valid steps
+  const bool use_tma = p.tma_ok != 0;
+  const bool tma_store = use_tma && n_ch == kCh;  // whole boxes stay in this batch
+  const bool has_z = p.z != nullptr;
+
+  float Av[kS], a2[kS];
+#pragma unroll
+  for (int j = 0; j < kS; ++j) {
+    Av[j] = __ldg(p.A + d * NS + q + kLPC * j);
+    a2[j] = Av[j] * kLog2e;
+  }
+  const float Dv = p.D ? __ldg(p.D + d) : 0.f;
+  const float bias = p.delta_bias ? __ldg(p.delta_bias + d) : 0.f;
+
+  // Steps past the last valid tile are padding: their gradients are zero.
+  {
+    const int tz = (k_last + 1) * kBT;
+    const bool vec = use_tma;  // 16-byte aligned rows (L * esize % 16 == 0)
+    zero_rows(static_cast<T*>(p.du), row0, n_ch, L, tz, vec, lane);
+    zero_rows(static_cast<T*>(p.ddelta), row0, n_ch, L, tz, vec, lane);
+    if (has_z) zero_rows(static_cast<T*>(p.dz), row0, n_ch, L, tz, vec, lane);
+  }
+
+  // TMA pipeline: position i of the walk is tile k_last - i; its arrays go
+  // to buffer i & 1 (bar[i & 1]), its pre-gate rows to the single rawP (barP,
+  // issued once the previous position's transform has read rawP).
+  constexpr uint32_t kChBytes = kCh * kBT * sizeof(T);
+  constexpr uint32_t kNBytes = NS * kBT * sizeof(T);
+  const int rc = static_cast<int>(row0);
+  auto issue = [&](int i) {  // one thread
+    const int s = i & 1;
+    const int x = (k_last - i) * kBT;
+    uint64_t* bar = &sh.bar[s];
+    mbar_arrive_expect_tx(bar, (has_z ? 4u : 3u) * kChBytes + 2u * kNBytes);
+    tma_load_2d(&sh.rawD[s][0][0], &maps.d, x, rc, bar);
+    tma_load_2d(&sh.rawU[s][0][0], &maps.u, x, rc, bar);
+    tma_load_2d(&sh.rawY[s][0][0], &maps.y, x, rc, bar);
+    if (has_z) tma_load_2d(&sh.rawZ[s][0][0], &maps.z, x, rc, bar);
+    tma_load_2d(&sh.rawB[s][0][0], &maps.b, x, b * NS, bar);
+    tma_load_2d(&sh.rawC[s][0][0], &maps.c, x, b * NS, bar);
+  };
+  auto issue_pre = [&](int i) {  // one thread
+    mbar_arrive_expect_tx(&sh.barP, kChBytes);
+    tma_load_2d(&sh.rawP[0][0], &maps.p, (k_last - i) * kBT, rc, &sh.barP);
+  };
+  if (use_tma && lane == 0) {
+    mbar_init(&sh.bar[0], 1);
+    mbar_init(&sh.bar[1], 1);
+    mbar_init(&sh.barP, 1);
+    fence_mbar_init();
+    if (k_last >= 0) {
+      issue(0);
+      if (has_z) issue_pre(0);
+    }
+    if (k_last >= 1) issue(1);
+  }
+  __syncwarp();
+
+  // Adjoint carries: g of the step after the current one and its a.
+  float gn[kS], an[kS];
+  float2 dAacc[kS];
+#pragma unroll
+  for (int j = 0; j < kS; ++j) {
+    gn[j] = (act && p.dlast) ? __ldg(p.dlast + row * NS + q + kLPC * j) : 0.f;
+    an[j] = 1.f;
+    dAacc[j] = make_float2(0.f, 0.f);
+  }
+  float dD_acc = 0.f, dbias_acc = 0.f;
+  const bool acc_aligned = (L & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.dB_acc) |
+                                              reinterpret_cast<uintptr_t>(p.dC_acc)) & 15) == 0;
+  float* dB_b = p.dB_acc + static_cast<size_t>(b) * NS * L;
+  float* dC_b = p.dC_acc + static_cast<size_t>(b) * NS * L;
+
+  for (int k = k_last; k >= 0; --k) {
+    const int i = k_last - k;
+    const int s = i & 1;
+    const int t0 = k * kBT;
+    T* bD = &sh.rawD[s][0][0];
+    T* bU = &sh.rawU[s][0][0];
+    T* bY = &sh.rawY[s][0][0];
+    T* bZ = &sh.rawZ[s][0][0];
+    const T* bB = &sh.rawB[s][0][0];
+    const T* bC = &sh.rawC[s][0][0];
+    // fp32 work rows: delta_eff and dy
+    float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
+    float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
+
+    // state entering the tile
+    float h_in[kS];
+#pragma unroll
+    for (int j = 0; j < kS; ++j) {
+      const int n = q + kLPC * j;
+      float v = 0.f;
+      if (act) {
+        if (k > 0)
+          v = p.chunk_states[(row * p.n_chunks + k - 1) * NS + n];
+        else if (p.h0)
+          v = __ldg(p.h0 + row * NS + n);
+      }
+      h_in[j] = v;
+    }
+
+    if (use_tma) {
+      bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
+      if (has_z) ok = ok && mbar_wait_bounded(&sh.barP, i & 1);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) {
+          atomicOr(&g_bwd_device_error, kErrTmaTimeout);
+          // let the copies in flight land before the CTA exits
+          mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
+          if (has_z) mbar_wait_bounded(&sh.barP, i & 1);
+          if (i == 0 && k >= 1) mbar_wait_bounded(&sh.bar[1], 0);
+          bulk_wait_all();
+        }
+        return;
+      }
+    } else {
+      stage_tile_plain(bD, static_cast<const T*>(p.delta), row0, n_ch, kCh, L, t0, lane);
+      stage_tile_plain(bU, static_cast<const T*>(p.u), row0, n_ch, kCh, L, t0, lane);
+      stage_tile_plain(bY, static_cast<const T*>(p.dout), row0, n_ch, kCh, L, t0, lane);
+      if (has_z) {
+        stage_tile_plain(bZ, static_cast<const T*>(p.z), row0, n_ch, kCh, L, t0, lane);
+        stage_tile_plain(&sh.rawP[0][0], static_cast<const T*>(p.out_pre), row0, n_ch, kCh, L,
+                         t0, lane);
+      }
+      const size_t brow = static_cast<size_t>(b) * NS;
+      stage_tile_plain(&sh.rawB[s][0][0], static_cast<const T*>(p.B), brow, NS, NS, L, t0, lane);
+      stage_tile_plain(&sh.rawC[s][0][0], static_cast<const T*>(p.C), brow, NS, NS, L, t0, lane);
+      __syncwarp();
+    }
+
+    // ---- 1. transform: lane (c, q) takes steps [q * kBT / kLPC, ...) of channel c
+    {
+      constexpr int kQ = kBT / 4 / kLPC;
+#pragma unroll
+      for (int qq = 0; qq < kQ; ++qq) {
+        const int tt = (q * kQ + qq) * 4;
+        const float4 x4 = ld4s(bD, c, tt);
+        const float4 u4 = ld4s(bU, c, tt);
+        const float4 y4 = ld4s(bY, c, tt);
+        float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f), p4 = z4;
+        if (has_z) {
+          z4 = ld4s(bZ, c, tt);
+          p4 = ld4s(&sh.rawP[0][0], c, tt);
+        }
+        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+        const float us[4] = {u4.x, u4.y, u4.z, u4.w};
+        const float ys[4] = {y4.x, y4.y, y4.z, y4.w};
+        const float zs[4] = {z4.x, z4.y, z4.z, z4.w};
+        const float ps[4] = {p4.x, p4.y, p4.z, p4.w};
+        float dl[4], dy[4], dz[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool valid = act && t0 + tt + e < len;
+          float xe = xs[e] + bias;
+          if (p.delta_softplus) xe = softplus_f(xe);
+          float ye = ys[e], ze = 0.f;
+          if (has_z) {
+            const float sz = sigmoid_f(zs[e]);
+            ze = ye * ps[e] * sz * fmaf(zs[e], 1.f - sz, 1.f);
+            ye *= zs[e] * sz;
+          }
+          dl[e] = valid ? xe : 0.f;
+          dy[e] = valid ? ye : 0.f;
+          dz[e] = valid ? ze : 0.f;
+          dD_acc = fmaf(dy[e], valid ? us[e] : 0.f, dD_acc);
+        }
+        st4s(wD, c, tt, make_float4(dl[0], dl[1], dl[2], dl[3]));
+        st4s(wY, c, tt, make_float4(dy[0], dy[1], dy[2], dy[3]));
+        if (has_z) st4s(bZ, c, tt, make_float4(dz[0], dz[1], dz[2], dz[3]));
+      }
+    }
+    __syncwarp();
+
+    if (use_tma && lane == 0 && k >= 1) {
+      fence_proxy_async_smem();  // the warp's reads of rawP are done
+      if (has_z) issue_pre(i + 1);
+      // the other buffer held the previous position's du/ddelta/dz for its
+      // bulk stores; once they have read it, refill it with position i + 1
+      if (i >= 1) {
+        bulk_wait_read_all();
+        issue(i + 1);
+      }
+    }
+
+    // u and delta_eff u (ZOH: u) of four steps; delta_eff is zero past the
+    // end, so delta_eff u is too (ZOH: b_bar = expm1(0) / A = 0)
+    auto load_dl_du = [&](int tg, float2 (&dlp)[2], float2 (&dup_)[2]) {
+      const float4 dl4 = ld4s(wD, c, tg);
+      const float4 u4 = ld4s(bU, c, tg);
+      dlp[0] = make_float2(dl4.x, dl4.y);
+      dlp[1] = make_float2(dl4.z, dl4.w);
+      dup_[0] = make_float2(u4.x, u4.y);
+      dup_[1] = make_float2(u4.z, u4.w);
+      if constexpr (!kZOH) {
+        dup_[0] = mul2(dup_[0], dlp[0]);
+        dup_[1] = mul2(dup_[1], dlp[1]);
+      }
+    };
+
+    // ---- 2. forward over the tile: the state entering each group
+    float hck[kNG][kS];
+    {
+      float h[kS];
+#pragma unroll
+      for (int j = 0; j < kS; ++j) h[j] = h_in[j];
+#pragma unroll
+      for (int g = 0; g < kNG; ++g) {
+#pragma unroll
+        for (int j = 0; j < kS; ++j) hck[g][j] = h[j];
+        if (g == kNG - 1) break;
+        const int tg = g * kGrp;
+        float2 dlp[2], dup_[2];
+        load_dl_du(tg, dlp, dup_);
+#pragma unroll
+        for (int j = 0; j < kS; ++j) {
+          const float4 B4 = ld4s(bB, q + kLPC * j, tg);
+          const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
+          const float2 a2p = dup2(a2[j]);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float2 arg = mul2(dlp[e], a2p);
+            const float2 ab = make_float2(ex2(arg.x), ex2(arg.y));
+            float2 bu;
+            if constexpr (kZOH) {
+              const float inv = 1.f / Av[j];
+              bu.x = Bp[e].x * (expm1f(dlp[e].x * Av[j]) * inv) * dup_[e].x;
+              bu.y = Bp[e].y * (expm1f(dlp[e].y * Av[j]) * inv) * dup_[e].y;
+            } else {
+              bu = mul2(Bp[e], dup_[e]);
+            }
+            h[j] = fmaf(ab.x, h[j], bu.x);
+            h[j] = fmaf(ab.y, h[j], bu.y);
+          }
+        }
+      }
+    }
+
+    // ---- 3. groups in reverse
+#pragma unroll
+    for (int g = kNG - 1; g >= 0; --g) {
+      const int tg = g * kGrp;
+      float2 dlp[2], dup_[2];
+      load_dl_du(tg, dlp, dup_);
+      const float4 dy4 = ld4s(wY, c, tg);
+      const float2 dyp[2] = {make_float2(dy4.x, dy4.y), make_float2(dy4.z, dy4.w)};
+      float2 gA[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g a h_{t-1} A
+      float2 gB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g B (ZOH: g b_bar)
+      float4 dCq[kS];
+#pragma unroll
+      for (int j = 0; j < kS; ++j) {
+        const int n = q + kLPC * j;
+        const float4 B4 = ld4s(bB, n, tg);
+        const float4 C4 = ld4s(bC, n, tg);
+        const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
+        const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
+        const float2 a2p = dup2(a2[j]);
+        // recompute a_t and h_t over the group
+        float2 ab[2], hv[2], bu[2], bb[2];
+        float hh = hck[g][j];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float2 arg = mul2(dlp[e], a2p);
+          ab[e] = make_float2(ex2(arg.x), ex2(arg.y));
+          if constexpr (kZOH) {
+            const float inv = 1.f / Av[j];
+            bb[e].x = expm1f(dlp[e].x * Av[j]) * inv;
+            bb[e].y = expm1f(dlp[e].y * Av[j]) * inv;
+            bu[e] = mul2(mul2(Bp[e], bb[e]), dup_[e]);
+          } else {
+            bu[e] = mul2(Bp[e], dup_[e]);
+          }
+          hv[e].x = hh = fmaf(ab[e].x, hh, bu[e].x);
+          hv[e].y = hh = fmaf(ab[e].y, hh, bu[e].y);
+        }
+        // adjoint, latest step first
+        const float2 e0 = mul2(dyp[0], Cp[0]), e1 = mul2(dyp[1], Cp[1]);
+        float2 gv[2];
+        gv[1].y = fmaf(an[j], gn[j], e1.y);
+        gv[1].x = fmaf(ab[1].y, gv[1].y, e1.x);
+        gv[0].y = fmaf(ab[1].x, gv[1].x, e0.y);
+        gv[0].x = fmaf(ab[0].y, gv[0].y, e0.x);
+        gn[j] = gv[0].x;
+        an[j] = ab[0].x;
+        float2 dBv[2], dCv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          // a_t h_{t-1} = h_t - b_t
+          const float2 ah = add2(hv[e], make_float2(-bu[e].x, -bu[e].y));
+          const float2 w = mul2(gv[e], ah);
+          gA[e] = fma2(w, dup2(Av[j]), gA[e]);
+          dAacc[j] = fma2(w, dlp[e], dAacc[j]);
+          if constexpr (kZOH) {
+            // d b_t/d delta = a_t B u, d b_t/d A = B u (delta a_t - b_bar) / A
+            const float2 gBu = mul2(gv[e], mul2(Bp[e], dup_[e]));
+            gA[e] = fma2(gBu, ab[e], gA[e]);
+            const float inv = 1.f / Av[j];
+            dAacc[j].x += gBu.x * (dlp[e].x * ab[e].x - bb[e].x) * inv;
+            dAacc[j].y += gBu.y * (dlp[e].y * ab[e].y - bb[e].y) * inv;
+            gB[e] = fma2(gv[e], mul2(Bp[e], bb[e]), gB[e]);
+            dBv[e] = mul2(gv[e], mul2(bb[e], dup_[e]));
+          } else {
+            gB[e] = fma2(gv[e], Bp[e], gB[e]);
+            dBv[e] = mul2(gv[e], dup_[e]);
+          }
+          dCv[e] = mul2(dyp[e], hv[e]);
+        }
+        sh.part[c][n ^ Cfg::part_swz(c)] = make_float4(dBv[0].x, dBv[0].y, dBv[1].x, dBv[1].y);
+        dCq[j] = make_float4(dCv[0].x, dCv[0].y, dCv[1].x, dCv[1].y);
+      }
+
+      // sum gA, gB over the channel's lanes (reduce-scatter: lane q keeps
+      // the steps it emits), then du and ddelta for those steps
+      const float fa[4] = {gA[0].x, gA[0].y, gA[1].x, gA[1].y};
+      const float fb[4] = {gB[0].x, gB[0].y, gB[1].x, gB[1].y};
+      auto emit = [&](int e, float sa, float sb) {
+        const int tl = tg + e;
+        const bool valid = act && t0 + tl < len;
+        const float dlv = ld1s(wD, c, tl);
+        const float dyv = ld1s(wY, c, tl);
+        const float uv = ld1s(bU, c, tl);
+        float gd = kZOH ? sa : fmaf(uv, sb, sa);
+        if (p.delta_softplus) gd *= sigmoid_from_softplus(dlv);
+        const float du = fmaf(Dv, dyv, kZOH ? sb : dlv * sb);
+        gd = valid ? gd : 0.f;
+        dbias_acc += gd;
+        st1s(bU, c, tl, valid ? du : 0.f);
+        st1s(bD, c, tl, gd);
+      };
+      if constexpr (kLPC == 4) {
+        const bool hi2 = (q & 2) != 0;
+        float ka0 = hi2 ? fa[2] : fa[0], ka1 = hi2 ? fa[3] : fa[1];
+        float kb0 = hi2 ? fb[2] : fb[0], kb1 = hi2 ? fb[3] : fb[1];
+        ka0 += __shfl_xor_sync(0xffffffffu, hi2 ? fa[0] : fa[2], 2);
+        ka1 += __shfl_xor_sync(0xffffffffu, hi2 ? fa[1] : fa[3], 2);
+        kb0 += __shfl_xor_sync(0xffffffffu, hi2 ? fb[0] : fb[2], 2);
+        kb1 += __shfl_xor_sync(0xffffffffu, hi2 ? fb[1] : fb[3], 2);
+        const bool hi1 = (q & 1) != 0;
+        float ka = hi1 ? ka1 : ka0, kb = hi1 ? kb1 : kb0;
+        ka += __shfl_xor_sync(0xffffffffu, hi1 ? ka0 : ka1, 1);
+        kb += __shfl_xor_sync(0xffffffffu, hi1 ? kb0 : kb1, 1);
+        emit(q, ka, kb);
+      } else if constexpr (kLPC == 2) {
+        const bool hi = (q & 1) != 0;
+        float ka0 = hi ? fa[2] : fa[0], ka1 = hi ? fa[3] : fa[1];
+        float kb0 = hi ? fb[2] : fb[0], kb1 = hi ? fb[3] : fb[1];
+        ka0 += __shfl_xor_sync(0xffffffffu, hi ? fa[0] : fa[2], 1);
+        ka1 += __shfl_xor_sync(0xffffffffu, hi ? fa[1] : fa[3], 1);
+        kb0 += __shfl_xor_sync(0xffffffffu, hi ? fb[0] : fb[2], 1);
+        kb1 += __shfl_xor_sync(0xffffffffu, hi ? fb[1] : fb[3], 1);
+        emit(2 * q, ka0, kb0);
+        emit(2 * q + 1, ka1, kb1);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) emit(e, fa[e], fb[e]);
+      }
+
+      // dB, then dC, of the group: sum the channels, add into the accumulators
+      const bool live = t0 + tg < len;  // warp-uniform
+      const bool whole = t0 + tg + kGrp <= len && acc_aligned;
+      __syncwarp();
+      if (live) flush_part<NS>(sh.part, dB_b, L, t0 + tg, len, whole, lane);
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kS; ++j) {
+        const int n = q + kLPC * j;
+        sh.part[c][n ^ Cfg::part_swz(c)] = dCq[j];
+      }
+      __syncwarp();
+      if (live) flush_part<NS>(sh.part, dC_b, L, t0 + tg, len, whole, lane);
+      __syncwarp();
+    }
+
+    // ---- 4. the tile's du, ddelta, dz
+    if (tma_store) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&maps.du, t0, rc, bU);
+        tma_store_2d(&maps.dd, t0, rc, bD);
+        if (has_z) tma_store_2d(&maps.dz, t0, rc, bZ);
+        bulk_commit();
+      }
+    } else {
+      unstage_tile_plain(static_cast<T*>(p.du), bU, row0, n_ch, L, t0, lane);
+      unstage_tile_plain(static_cast<T*>(p.ddelta), bD, row0, n_ch, L, t0, lane);
+      if (has_z) unstage_tile_plain(static_cast<T*>(p.dz), bZ, row0, n_ch, L, t0, lane);
+      __syncwarp();
+    }
+  }
+  if (use_tma && lane == 0) bulk_wait_all();
+
+  // ---- per-row results
+#pragma unroll
+  for (int m = 1; m < kLPC; m <<= 1) {
+    dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, m);
+    dbias_acc += __shfl_xor_sync(0xffffffffu, dbias_acc, m);
+  }
+  if (act) {
+#pragma unroll
+    for (int j = 0; j < kS; ++j) {
+      const int n = q + kLPC * j;
+      p.dA_part[row * NS + n] = dAacc[j].x + dAacc[j].y;
+      if (p.dh0) p.dh0[row * NS + n] = an[j] * gn[j];
+    }
+    if (q == 0) {
+      p.dD_part[row] = dD_acc;
+      p.dbias_part[row] = dbias_acc;
+    }
+  }
+}
+
 // Sums the per-batch partials of dA (dim*dstate), dD and ddelta_bias (dim)
 // in a fixed order, so these three are bitwise reproducible.
 __global__ void reduce_params_kernel(const float* __restrict__ dA_part,
@@ -717,6 +1340,104 @@ static bool encode_runs(CUtensorMap* m, const void* base, int io_dtype, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static cudaError_t launch_bwd_finish(const BwdParams& p, int dstate, int io_dtype,
+                                     void* dB_out, void* dC_out, float* dA, float* dD,
+                                     float* ddelta_bias, cudaStream_t stream);
+
+template <int NS, typename T, bool kZOH>
+static cudaError_t launch_bwd_tile_t(const BwdParams& p, const TileMaps& maps,
+                                     cudaStream_t stream) {
+  // the bytes in use: sizeof() would round up to the 1024-byte alignment
+  using Sh = TileShared<NS, T>;
+  const size_t smem = offsetof(Sh, barP) + sizeof(uint64_t);
+  auto kern = ss_bwd_tile_kernel<NS, T, kZOH>;
+  cudaError_t e = cudaFuncSetAttribute(
+      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.dim + TileCfg<NS>::kCh - 1) / TileCfg<NS>::kCh, p.batch);
+  kern<<<grid, 32, smem, stream>>>(p, maps);
+  return cudaPeekAtLastError();
+}
+
+template <typename T, bool kZOH>
+static cudaError_t launch_bwd_tile_n(const BwdParams& p, const TileMaps& maps, int dstate,
+                                     cudaStream_t stream) {
+  switch (dstate) {
+    case 1: return launch_bwd_tile_t<1, T, kZOH>(p, maps, stream);
+    case 2: return launch_bwd_tile_t<2, T, kZOH>(p, maps, stream);
+    case 4: return launch_bwd_tile_t<4, T, kZOH>(p, maps, stream);
+    case 8: return launch_bwd_tile_t<8, T, kZOH>(p, maps, stream);
+    case 16: return launch_bwd_tile_t<16, T, kZOH>(p, maps, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+static int tile_channels(int dstate) {
+  switch (dstate) {
+    case 1: return TileCfg<1>::kCh;
+    case 2: return TileCfg<2>::kCh;
+    case 4: return TileCfg<4>::kCh;
+    case 8: return TileCfg<8>::kCh;
+    default: return TileCfg<16>::kCh;
+  }
+}
+
+// A row-major (rows x L) operand in boxes of box_rows rows x kBT steps,
+// 128-byte swizzle for fp32 rows, 64-byte for bf16 (TileShared's layout).
+static bool encode_tile(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
+                        uint64_t L, uint32_t box_rows) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
+  const cuuint64_t dims[2] = {L, rows};
+  const cuuint64_t strides[1] = {L * esize};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBT), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, io_dtype == MSS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+            2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            io_dtype == MSS_BF16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static cudaError_t launch_bwd_tile(const BwdParams& p, int dstate, int io_dtype, int zoh,
+                                   cudaStream_t stream) {
+  BwdParams pk = p;
+  TileMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
+  const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  pk.tma_ok = (p.seqlen * esize) % 16 == 0 && al16(p.B) && al16(p.C) && al16(p.u) &&
+              al16(p.delta) && al16(p.dout) && al16(p.du) && al16(p.ddelta) &&
+              (!p.z || (al16(p.z) && al16(p.dz) && al16(p.out_pre)));
+  if (pk.tma_ok) {
+    const uint64_t brows = static_cast<uint64_t>(p.batch) * dstate;
+    const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
+    const uint64_t L = p.seqlen;
+    const uint32_t ch = static_cast<uint32_t>(tile_channels(dstate));
+    const uint32_t ns = static_cast<uint32_t>(dstate);
+    pk.tma_ok = encode_tile(&maps.b, p.B, io_dtype, brows, L, ns) &&
+                encode_tile(&maps.c, p.C, io_dtype, brows, L, ns) &&
+                encode_tile(&maps.u, p.u, io_dtype, rows, L, ch) &&
+                encode_tile(&maps.d, p.delta, io_dtype, rows, L, ch) &&
+                encode_tile(&maps.y, p.dout, io_dtype, rows, L, ch) &&
+                encode_tile(&maps.du, p.du, io_dtype, rows, L, ch) &&
+                encode_tile(&maps.dd, p.ddelta, io_dtype, rows, L, ch) &&
+                (!p.z || (encode_tile(&maps.z, p.z, io_dtype, rows, L, ch) &&
+                          encode_tile(&maps.p, p.out_pre, io_dtype, rows, L, ch) &&
+                          encode_tile(&maps.dz, p.dz, io_dtype, rows, L, ch)));
+  }
+  if (io_dtype == MSS_BF16)
+    return zoh ? launch_bwd_tile_n<__nv_bfloat16, true>(pk, maps, dstate, stream)
+               : launch_bwd_tile_n<__nv_bfloat16, false>(pk, maps, dstate, stream);
+  return zoh ? launch_bwd_tile_n<float, true>(pk, maps, dstate, stream)
+             : launch_bwd_tile_n<float, false>(pk, maps, dstate, stream);
+}
+
+static bool use_chunk_kernel() {
+  const char* v = getenv("MAMBA_SS_BWD_KERNEL");
+  return v && strcmp(v, "chunk") == 0;
+}
+
 cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream) {
@@ -725,6 +1446,12 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(p.dC_acc, 0, n_bnl * sizeof(float), stream);
   if (e != cudaSuccess) return e;
+
+  if (!use_chunk_kernel()) {
+    e = launch_bwd_tile(p, dstate, io_dtype, zoh, stream);
+    if (e != cudaSuccess) return e;
+    return launch_bwd_finish(p, dstate, io_dtype, dB_out, dC_out, dA, dD, ddelta_bias, stream);
+  }
 
   BwdParams pk = p;
   BwdMaps maps;
@@ -757,7 +1484,16 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
             : launch_bwd_n<float, false>(pk, maps, dstate, stream);
   }
   if (e != cudaSuccess) return e;
+  return launch_bwd_finish(p, dstate, io_dtype, dB_out, dC_out, dA, dD, ddelta_bias, stream);
+}
 
+// The batch reduction of the parameter gradients and (bf16 I/O) the
+// fp32 -> bf16 conversion of dB/dC, after either backward kernel.
+static cudaError_t launch_bwd_finish(const BwdParams& p, int dstate, int io_dtype,
+                                     void* dB_out, void* dC_out, float* dA, float* dD,
+                                     float* ddelta_bias, cudaStream_t stream) {
+  const size_t n_bnl = static_cast<size_t>(p.batch) * dstate * p.seqlen;
+  cudaError_t e = cudaSuccess;
   {
     const int total = p.dim * dstate + 2 * p.dim;
     const int threads = 256;

@@ -47,7 +47,7 @@ mss_status check_dims(const char* op, int io_dtype, int discretization,
   return MSS_OK;
 }
 
-int n_chunks_of(int length) { return (length + mss::kChunk - 1) / mss::kChunk; }
+int n_chunks_of(int length) { return (length + mss::kCkpt - 1) / mss::kCkpt; }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 

@@ -22,12 +22,13 @@
 namespace mss {
 
 constexpr int kItems = 16;                  // steps per lane per chunk
-constexpr int kChunk = 32 * kItems;         // steps per chunk (== MSS_CHUNK)
-static_assert(kChunk == MSS_CHUNK, "chunk size must match the public header");
+constexpr int kChunk = 32 * kItems;         // steps per chunk of the warp-scan backward
+constexpr int kCkpt = MSS_CHUNK;            // steps per saved carry (chunk_states entry)
+static_assert(kChunk % kCkpt == 0, "a chunk ends on a saved carry");
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct FwdParams {
-  int batch, dim, seqlen, n_chunks;
+  int batch, dim, seqlen, n_chunks;  // n_chunks: saved carries per row, ceil(L / kCkpt)
   int delta_softplus;
   int tma_ok;  // rows may be staged with TMA bulk copies (set by the launcher)
   const void* u;
@@ -309,6 +310,15 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, int x, int y, int
       "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
           reinterpret_cast<uint64_t>(tmap)),
       "r"(x), "r"(y), "r"(z), "r"(smem_u32(src))
+      : "memory");
+}
+// 2-D TMA tile store shared -> global (elements outside the tensor are not
+// written); completion is tracked by the issuing thread's bulk async-groups.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* src) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(x), "r"(y), "r"(smem_u32(src))
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit() {

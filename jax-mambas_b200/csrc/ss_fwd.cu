@@ -23,7 +23,7 @@
 //      kS-state partial sums of C_t h_t are reduced over the channel's lanes;
 //   3. emit: out = (y + D u) * silu(z) and the pre-gate y + D u (read by the
 //      backward for dz) are written coalesced.
-// The state at every MSS_CHUNK boundary is saved for the backward. Rows whose
+// The state at the end of every tile (MSS_CHUNK steps) is saved for the backward. Rows whose
 // length or base address is not 16-byte aligned take the same path with the
 // staging done by plain loads instead of TMA.
 #include <cudaTypedefs.h>
@@ -40,7 +40,7 @@ __device__ unsigned int g_fwd_device_error = 0;
 constexpr int kTile = 32;  // steps staged per pass
 constexpr int kPad = 4;    // row padding (floats) of the fp32 work tiles
 constexpr int kRow = kTile + kPad;
-static_assert(kChunk % kTile == 0, "a carry checkpoint must end a tile");
+static_assert(kCkpt == kTile, "a carry is saved at the end of every tile");
 
 template <int NS>
 struct FwdCfg {
@@ -349,13 +349,11 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       }
     }
 
-    // ---- carry checkpoint at the end of every chunk (and of the sequence)
-    const int t_end = t0 + kTile;
-    if (lane_active && (t_end % kChunk == 0 || t_end >= L)) {
-      const int c = (t_end - 1) / kChunk;
+    // ---- carry checkpoint at the end of every tile
+    if (lane_active) {
 #pragma unroll
       for (int j = 0; j < kS; ++j)
-        p.chunk_states[(row * p.n_chunks + c) * NS + q + kLPC * j] = h[j];
+        p.chunk_states[(row * p.n_chunks + k) * NS + q + kLPC * j] = h[j];
     }
     __syncthreads();
 
