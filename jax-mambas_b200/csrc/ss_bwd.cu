@@ -699,7 +699,8 @@ struct TileShared {
   // bf16 I/O: fp32 work rows delta_eff and dy, swizzled like fp32 staging
   alignas(16) float wD[kInPlace ? 1 : kCh][kBT];
   alignas(16) float wY[kInPlace ? 1 : kCh][kBT];
-  float4 part[kCh][NS];  // one group's dB or dC per (channel, swizzled state)
+  // one group's dB or dC per (channel, swizzled state); N = 16 sums by shuffles
+  float4 part[NS == 16 ? 1 : kCh][NS];
   uint64_t bar[2];
   uint64_t barP;
 };
@@ -781,6 +782,14 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, bool vec
   }
 }
 
+// acc += the partner lane's (lane ^ m) v, component-wise.
+__device__ __forceinline__ void add_xor4(float4& acc, const float4& v, int m) {
+  acc.x += __shfl_xor_sync(0xffffffffu, v.x, m);
+  acc.y += __shfl_xor_sync(0xffffffffu, v.y, m);
+  acc.z += __shfl_xor_sync(0xffffffffu, v.z, m);
+  acc.w += __shfl_xor_sync(0xffffffffu, v.w, m);
+}
+
 // Sums one group's [channel][state] tile over the channels and adds state
 // row n's four steps into acc_b[n * L + t] (t = the group's first step).
 // Lane o + NS*h sums channels h*kS .. h*kS + kS - 1 of state o, then the
@@ -840,6 +849,13 @@ __global__ void __launch_bounds__(32)
   const int d = d0 + (act ? c : 0);
   const size_t row = static_cast<size_t>(b) * p.dim + d;
   const size_t row0 = static_cast<size_t>(b) * p.dim + d0;  // first row of the CTA
+  // N = 16: dB/dC are summed over the warp's 8 channels by a shuffle
+  // reduce-scatter. Lane slot j holds state q + 4 (j ^ perm), perm taken from
+  // channel bits 1 and 2, so that the first two shuffle levels exchange the
+  // same slots on every lane.
+  constexpr bool kShflFlush = NS == 16;
+  const int perm = kShflFlush ? (c >> 1) & 3 : 0;
+  auto st_of = [&](int j) { return q + kLPC * (j ^ perm); };
 
   int len = L;
   if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
@@ -851,7 +867,7 @@ __global__ void __launch_bounds__(32)
   float Av[kS], a2[kS];
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
-    Av[j] = __ldg(p.A + d * NS + q + kLPC * j);
+    Av[j] = __ldg(p.A + d * NS + st_of(j));
     a2[j] = Av[j] * kLog2e;
   }
   const float Dv = p.D ? __ldg(p.D + d) : 0.f;
@@ -906,7 +922,7 @@ __global__ void __launch_bounds__(32)
   float2 dAacc[kS];
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
-    gn[j] = (act && p.dlast) ? __ldg(p.dlast + row * NS + q + kLPC * j) : 0.f;
+    gn[j] = (act && p.dlast) ? __ldg(p.dlast + row * NS + st_of(j)) : 0.f;
     an[j] = 1.f;
     dAacc[j] = make_float2(0.f, 0.f);
   }
@@ -934,7 +950,7 @@ __global__ void __launch_bounds__(32)
     float h_in[kS];
 #pragma unroll
     for (int j = 0; j < kS; ++j) {
-      const int n = q + kLPC * j;
+      const int n = st_of(j);
       float v = 0.f;
       if (act) {
         if (k > 0)
@@ -1059,7 +1075,7 @@ __global__ void __launch_bounds__(32)
         load_dl_du(tg, dlp, dup_);
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
-          const float4 B4 = ld4s(bB, q + kLPC * j, tg);
+          const float4 B4 = ld4s(bB, st_of(j), tg);
           const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
           const float2 a2p = dup2(a2[j]);
 #pragma unroll
@@ -1091,10 +1107,10 @@ __global__ void __launch_bounds__(32)
       const float2 dyp[2] = {make_float2(dy4.x, dy4.y), make_float2(dy4.z, dy4.w)};
       float2 gA[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g a h_{t-1} A
       float2 gB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g B (ZOH: g b_bar)
-      float4 dCq[kS];
+      float4 dBq[kS], dCq[kS];
 #pragma unroll
       for (int j = 0; j < kS; ++j) {
-        const int n = q + kLPC * j;
+        const int n = st_of(j);
         const float4 B4 = ld4s(bB, n, tg);
         const float4 C4 = ld4s(bC, n, tg);
         const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
@@ -1150,8 +1166,18 @@ __global__ void __launch_bounds__(32)
           }
           dCv[e] = mul2(dyp[e], hv[e]);
         }
-        sh.part[c][n ^ Cfg::part_swz(c)] = make_float4(dBv[0].x, dBv[0].y, dBv[1].x, dBv[1].y);
+        dBq[j] = make_float4(dBv[0].x, dBv[0].y, dBv[1].x, dBv[1].y);
         dCq[j] = make_float4(dCv[0].x, dCv[0].y, dCv[1].x, dCv[1].y);
+        if constexpr (kShflFlush) {
+          // level 1 (channel bit 2): slots 2, 3 go to the partner, whose
+          // slots 0, 1 hold the same states
+          if (j >= 2) {
+            add_xor4(dBq[j - 2], dBq[j], 16);
+            add_xor4(dCq[j - 2], dCq[j], 16);
+          }
+        } else {
+          sh.part[c][n ^ Cfg::part_swz(c)] = dBq[j];
+        }
       }
 
       // sum gA, gB over the channel's lanes (reduce-scatter: lane q keeps
@@ -1200,20 +1226,41 @@ __global__ void __launch_bounds__(32)
         for (int e = 0; e < 4; ++e) emit(e, fa[e], fb[e]);
       }
 
-      // dB, then dC, of the group: sum the channels, add into the accumulators
+      // dB and dC of the group: sum the channels, add into the accumulators
       const bool live = t0 + tg < len;  // warp-uniform
       const bool whole = t0 + tg + kGrp <= len && acc_aligned;
-      __syncwarp();
-      if (live) flush_part<NS>(sh.part, dB_b, L, t0 + tg, len, whole, lane);
-      __syncwarp();
+      if constexpr (kShflFlush) {
+        // level 2 (channel bit 1): slot 1 to the partner; level 3 (bit 0):
+        // lanes with bit 0 clear keep dB, the others dC, of state st_of(0)
+        add_xor4(dBq[0], dBq[1], 8);
+        add_xor4(dCq[0], dCq[1], 8);
+        const bool b0 = (c & 1) != 0;
+        float4 keep = b0 ? dCq[0] : dBq[0];
+        add_xor4(keep, b0 ? dBq[0] : dCq[0], 4);
+        if (live) {
+          float* gp = (b0 ? dC_b : dB_b) + static_cast<size_t>(st_of(0)) * L + t0 + tg;
+          if (whole) {
+            atomicAdd(reinterpret_cast<float4*>(gp), keep);
+          } else {
+            const float e4[4] = {keep.x, keep.y, keep.z, keep.w};
 #pragma unroll
-      for (int j = 0; j < kS; ++j) {
-        const int n = q + kLPC * j;
-        sh.part[c][n ^ Cfg::part_swz(c)] = dCq[j];
+            for (int e = 0; e < 4; ++e)
+              if (t0 + tg + e < len) atomicAdd(gp + e, e4[e]);
+          }
+        }
+      } else {
+        __syncwarp();
+        if (live) flush_part<NS>(sh.part, dB_b, L, t0 + tg, len, whole, lane);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kS; ++j) {
+          const int n = st_of(j);
+          sh.part[c][n ^ Cfg::part_swz(c)] = dCq[j];
+        }
+        __syncwarp();
+        if (live) flush_part<NS>(sh.part, dC_b, L, t0 + tg, len, whole, lane);
+        __syncwarp();
       }
-      __syncwarp();
-      if (live) flush_part<NS>(sh.part, dC_b, L, t0 + tg, len, whole, lane);
-      __syncwarp();
     }
 
     // ---- 4. the tile's du, ddelta, dz
@@ -1244,7 +1291,7 @@ __global__ void __launch_bounds__(32)
   if (act) {
 #pragma unroll
     for (int j = 0; j < kS; ++j) {
-      const int n = q + kLPC * j;
+      const int n = st_of(j);
       p.dA_part[row * NS + n] = dAacc[j].x + dAacc[j].y;
       if (p.dh0) p.dh0[row * NS + n] = an[j] * gn[j];
     }
