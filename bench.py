@@ -120,7 +120,7 @@ def _algorithmic(cfg, esize, d=None):
     d = cfg["dim"] if d is None else d
     elems = b * d * L
     bnl = b * n * L
-    nch = math.ceil(L / 32)  # saved carries per row (one per 32-step tile)
+    nch = math.ceil(L / 4)  # saved carries per row (one per 4 steps)
     cs = b * d * nch * n * 4
     # forward: u, delta, z in; out and the pre-gate out (kept for dz) out
     fwd = elems * 5 * esize + 2 * bnl * esize + cs

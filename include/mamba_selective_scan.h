@@ -15,7 +15,8 @@
  *   A, dA ...................................... (dim, dstate)        fp32
  *   D, delta_bias, dD, ddelta_bias ............. (dim)                fp32
  *   initial_state, last_state, d_* ............. (batch, dim, dstate) fp32
- *   chunk_states ............................... (batch, dim, n_chunks, dstate) fp32
+ *   chunk_states ............................... batch*n_chunks*dim*dstate fp32,
+ *                                                  16-byte aligned; layout private
  *   seq_lens ................................... (batch) int32
  * These are the physical layouts the reference pins through its ffi_call
  * input_layouts/output_layouts (mamba/selective_scan_cuda.py:138-146,180-198).
@@ -41,7 +42,7 @@ typedef enum { MSS_F32 = 0, MSS_BF16 = 1 } mss_dtype;
 typedef enum { MSS_EULER = 0, MSS_ZOH = 1 } mss_discretization;
 
 /* Time steps covered by one saved carry (one entry of chunk_states). */
-#define MSS_CHUNK 32
+#define MSS_CHUNK 4
 
 /* Message of the last failed call on this host thread ("" if none). */
 const char* mamba_ss_last_error(void);
@@ -55,7 +56,7 @@ const char* mamba_ss_version(void);
  * reference, whose kernels have no waits. */
 uint32_t mamba_ss_take_device_error(void);
 
-/* Number of fp32 elements of chunk_states: batch*dim*ceil(length/32)*dstate.
+/* Number of fp32 elements of chunk_states: batch*dim*ceil(length/4)*dstate.
  * The reference sizes the same residual (batch, dim, ceil(L/2048), N, 2)
  * (mamba/selective_scan_cuda.py:129-134); it is private to the custom_vjp. */
 int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,

@@ -6,23 +6,9 @@
 // softplus(delta + bias), D skip and silu(z) gate, and the ZOH discretization
 // the reference leaves to JAX autodiff (mamba/selective_scan_cuda.py:250-256).
 //
-// Per (batch, channel) row a warp walks the chunks in reverse. For each chunk
-// and state it
-//   1. recomputes h_t over the chunk from the saved carry (forward scan),
-//   2. runs the adjoint recurrence g_t = dy_t C_t + a_{t+1} g_{t+1} as a
-//      reverse warp scan seeded with the carry from the later chunk,
-//   3. accumulates, per step, sum_n g B (-> du, and the u-part of ddelta),
-//      sum_n g a h_{t-1} A (-> ddelta), per lane dA, and the cross-channel
-//      sums dB = g delta u and dC = dy h in a shared-memory tile.
-// dz uses the pre-gate output y + D u saved by the forward.
-// The warps of a CTA (kBwdWarps channels of one batch) take the states in
-// lockstep. Each state's B and C rows for the chunk are staged once per CTA
-// by a 3-D tensor-map TMA copy whose 64-byte (fp32) / 32-byte (bf16) swizzle
-// makes every lane's 16-step run a conflict-free shared-memory read; the copy
-// of the next state flies while this one computes. dB/dC sum over channels:
-// each warp writes its rows to shared memory, the CTA adds the kBwdWarps rows
-// and adds the result to the fp32 accumulators in global memory with 16-byte
-// atomics.
+// The scan kernel (ss_bwd_tile_kernel) is described below; after it,
+// reduce_params_kernel sums the per-batch dA, dD and ddelta_bias partials in a
+// fixed order and, for bf16 I/O, f32_to_bf16_kernel narrows dB and dC.
 #include <algorithm>
 #include <cstddef>
 #include <cstdlib>
@@ -35,622 +21,21 @@ namespace mss {
 
 __device__ unsigned int g_bwd_device_error = 0;
 
-constexpr int kBwdWarps = 4;
-constexpr int kHalf = kItems / 2;
-
-// Float4 slot of logical float4 group q (q = t_in_chunk / 4) in a shared tile
-// row. Lane i writes the four groups 4i..4i+3; XOR-ing the group index with
-// (i >> 1) & 3 spreads each quarter-warp of 128-bit accesses over all banks.
-__device__ __forceinline__ int tile_slot(int q) {
-  const int i = q >> 2;
-  return (i << 2) | ((q & 3) ^ ((i >> 1) & 3));
-}
-
-// Tensor maps of the TMA-staged B and C (see launch_bwd).
-struct BwdMaps {
-  CUtensorMap b, c;                    // [rows = batch*dstate][L/16][16]
-  CUtensorMap u, d, z, dout, pre;      // [rows = batch*dim][L/16][16], loads
-  CUtensorMap du, dd, dz;              // same shape, stores
-};
-
-template <int NS, typename T>
-struct BwdShared {
-  // one state's B and C for a chunk: 32 lane runs of kItems steps (swizzled)
-  alignas(1024) T bufB[2][32][kItems];
-  alignas(1024) T bufC[2][32][kItems];
-  // this chunk's u and delta runs per warp (swizzled like B/C); reused to
-  // stage du and ddelta for the TMA stores
-  alignas(1024) T arrU[kBwdWarps][32][kItems];
-  alignas(1024) T arrD[kBwdWarps][32][kItems];
-  // per-warp dB/dC rows of the current state, in tile_slot order. Before the
-  // state loop the same bytes hold the chunk's z, dout and pre-gate runs
-  // (zone offsets 0, kArr and half of wrow); dz is staged in the pre-gate slot,
-  // which lies in the half used from the second state on.
-  alignas(1024) float4 wrow[2][kBwdWarps][2][kChunk / 4];
-  float gcarry[kBwdWarps][NS];
-  float Aw[kBwdWarps][NS];   // A of each warp's channel
-  float hsw[kBwdWarps][NS];  // state entering the current chunk, per warp
-  float dA[kBwdWarps][NS][32];
-  uint64_t bar[3];
-  static constexpr int kArr = kBwdWarps * 32 * kItems;  // elements per chunk array
-  __device__ T (*zone(int k))[32][kItems] {
-    unsigned char* base = reinterpret_cast<unsigned char*>(&wrow[0][0][0][0]);
-    const size_t off = k == 0 ? 0 : k == 1 ? kArr * sizeof(T) : sizeof(wrow) / 2;
-    return reinterpret_cast<T(*)[32][kItems]>(base + off);
-  }
-};
-// z and dout fit the first half of wrow, the pre-gate runs the second half
-static_assert(2 * kBwdWarps * 32 * kItems * 4 <= kBwdWarps * 2 * (kChunk / 4) * 16,
-              "zone fits wrow");
-
-// Staged B/C rows hold 32 lane runs of kItems steps. fp32 runs are 64 bytes
-// with the TMA's 64-byte swizzle (16-byte chunk j of run r sits at chunk
-// j ^ ((r >> 1) & 3)); bf16 runs are 32 bytes with the 32-byte swizzle
-// (chunk j at j ^ ((r >> 2) & 1)). Either way a warp reading one chunk per
-// lane touches every bank once.
-__device__ __forceinline__ int swz_chunk(int lane, int j, int esize) {
-  return esize == 4 ? (j ^ ((lane >> 1) & 3)) : (j ^ ((lane >> 2) & 1));
-}
-
-// Pairs 2j and 2j+1 (steps 4j .. 4j+3) of lane `lane`'s run.
-__device__ __forceinline__ void lds_quad(const float (*buf)[kItems], int lane, int j,
-                                         float2 (&v)[2]) {
-  const float4 f = *reinterpret_cast<const float4*>(buf[lane] + 4 * swz_chunk(lane, j, 4));
-  v[0] = make_float2(f.x, f.y);
-  v[1] = make_float2(f.z, f.w);
-}
-__device__ __forceinline__ void lds_quad(const __nv_bfloat16 (*buf)[kItems], int lane, int j,
-                                         float2 (&v)[2]) {
-  const uint2 w = *reinterpret_cast<const uint2*>(buf[lane] + 8 * swz_chunk(lane, j >> 1, 2) +
-                                                  4 * (j & 1));
-  v[0] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-  v[1] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-}
-
-template <typename T>
-__device__ __forceinline__ void lds_run16(const T (*buf)[kItems], int lane,
-                                          float2 (&v)[kItems / 2]) {
-#pragma unroll
-  for (int j = 0; j < kItems / 4; ++j) {
-    float2 q[2];
-    lds_quad(buf, lane, j, q);
-    v[2 * j] = q[0];
-    v[2 * j + 1] = q[1];
-  }
-}
-
-__device__ __forceinline__ void sts_quad(float (*buf)[kItems], int lane, int j, float2 a,
-                                         float2 b) {
-  *reinterpret_cast<float4*>(buf[lane] + 4 * swz_chunk(lane, j, 4)) = make_float4(a.x, a.y, b.x, b.y);
-}
-__device__ __forceinline__ void sts_quad(__nv_bfloat16 (*buf)[kItems], int lane, int j,
-                                         float2 a, float2 b) {
-  uint2 w;
-  *reinterpret_cast<__nv_bfloat162*>(&w.x) = __floats2bfloat162_rn(a.x, a.y);
-  *reinterpret_cast<__nv_bfloat162*>(&w.y) = __floats2bfloat162_rn(b.x, b.y);
-  *reinterpret_cast<uint2*>(buf[lane] + 8 * swz_chunk(lane, j >> 1, 2) + 4 * (j & 1)) = w;
-}
-template <typename T>
-__device__ __forceinline__ void sts_run16(T (*buf)[kItems], int lane,
-                                          const float2 (&v)[kItems / 2]) {
-#pragma unroll
-  for (int j = 0; j < kItems / 4; ++j) sts_quad(buf, lane, j, v[2 * j], v[2 * j + 1]);
-}
-
-// Fills one state's staged B/C rows for the chunk at t0 with plain loads
-// (rows that TMA cannot serve), in the same swizzled layout; steps at or past
-// `len` read as zero. Called by the whole CTA.
-template <typename T>
-__device__ void stage_bc_plain(T (*bB)[kItems], T (*bC)[kItems], const T* Bn, const T* Cn,
-                               int t0, int len) {
-  for (int i = threadIdx.x; i < 2 * kChunk; i += blockDim.x) {
-    const int which = i / kChunk, k = i % kChunk;
-    const int t = t0 + k;
-    const T* src = which ? Cn : Bn;
-    const T v = t < len ? src[t] : T(0.f);
-    const int r = k / kItems, e = k % kItems;
-    constexpr int kPerChunk = 16 / sizeof(T);
-    const int pos = kPerChunk * swz_chunk(r, e / kPerChunk, sizeof(T)) + e % kPerChunk;
-    (which ? bC : bB)[r][pos] = v;
-  }
-}
-
-template <int NS, typename T, bool kZOH>
-__global__ void __launch_bounds__(kBwdWarps * 32, 3)
-    ss_bwd_kernel(const BwdParams p, const __grid_constant__ BwdMaps maps) {
-  using Sh = BwdShared<NS, T>;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int d = blockIdx.x * kBwdWarps + warp;
-  const int b = blockIdx.y;
-  const bool active = d < p.dim;
-  const int dc = active ? d : 0;  // clamp for parameter loads
-
-  const int L = p.seqlen;
-  const size_t row = static_cast<size_t>(b) * p.dim + dc;
-  const T* u_row = static_cast<const T*>(p.u) + row * L;
-  const T* dl_row = static_cast<const T*>(p.delta) + row * L;
-  const T* z_row = p.z ? static_cast<const T*>(p.z) + row * L : nullptr;
-  const T* dout_row = static_cast<const T*>(p.dout) + row * L;
-  T* du_row = static_cast<T*>(p.du) + row * L;
-  T* ddl_row = static_cast<T*>(p.ddelta) + row * L;
-  T* dz_row = p.dz ? static_cast<T*>(p.dz) + row * L : nullptr;
-  const T* B_b = static_cast<const T*>(p.B) + static_cast<size_t>(b) * NS * L;
-  const T* C_b = static_cast<const T*>(p.C) + static_cast<size_t>(b) * NS * L;
-
-  int len = L;
-  if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
-  const int lim = active ? len : 0;  // inactive warps see zeros
-  const float Dv = p.D ? __ldg(p.D + dc) : 0.f;
-  const float bias = p.delta_bias ? __ldg(p.delta_bias + dc) : 0.f;
-
-  const bool use_tma = p.tma_ok != 0;
-  // chunks at or past `len` are padding only and skipped; the TMA pipeline
-  // walks (chunk, state) for the others, chunks in reverse
-  const int n_big = (L + kChunk - 1) / kChunk;  // chunks of kChunk steps
-  const int c_first = len > 0 ? min(n_big - 1, (len - 1) / kChunk) : -1;
-  auto issue = [&](int c, int n, int seq) {  // one thread
-    uint64_t* bar = &sh.bar[seq & 1];
-    mbar_arrive_expect_tx(bar, 2u * 32u * kItems * sizeof(T));
-    const int y = c * (kChunk / kItems);
-    tma_load_3d(&sh.bufB[seq & 1][0][0], &maps.b, 0, y, b * NS + n, bar);
-    tma_load_3d(&sh.bufC[seq & 1][0][0], &maps.c, 0, y, b * NS + n, bar);
-  };
-  // TMA stores write whole boxes of kBwdWarps rows: only CTAs whose rows all
-  // belong to this batch may use them (a tail CTA would spill into the next).
-  const bool tma_store = use_tma && (blockIdx.x + 1) * kBwdWarps <= p.dim;
-  const int row0 = b * p.dim + blockIdx.x * kBwdWarps;  // first (batch, channel) row
-  if (use_tma && threadIdx.x == 0) {
-    mbar_init(&sh.bar[0], 1);
-    mbar_init(&sh.bar[1], 1);
-    mbar_init(&sh.bar[2], 1);
-    fence_mbar_init();
-    if (c_first >= 0) issue(c_first, 0, 0);
-  }
-
-  // Seed the adjoint carries, clear the dA partials.
-  if (lane < NS) {
-    sh.gcarry[warp][lane] =
-        (active && p.dlast) ? __ldg(p.dlast + row * NS + lane) : 0.f;
-  }
-#pragma unroll
-  for (int n = 0; n < NS; ++n) sh.dA[warp][n][lane] = 0.f;
-  __syncthreads();
-
-  float dD_acc = 0.f, dbias_acc = 0.f;
-
-  // dB/dC flush: each thread owns the same kFlushPerThread float4 groups of
-  // every state's rows; their shared-memory slots are fixed.
-  constexpr int kFlushPerThread = 2 * (kChunk / 4) / (kBwdWarps * 32);
-  static_assert(kFlushPerThread * kBwdWarps * 32 == 2 * (kChunk / 4), "flush split");
-  int flush_slot[kFlushPerThread];
-#pragma unroll
-  for (int k = 0; k < kFlushPerThread; ++k)
-    flush_slot[k] = tile_slot((threadIdx.x + k * kBwdWarps * 32) % (kChunk / 4));
-  // 16-byte atomics need 16-byte aligned accumulator rows (L % 4 == 0)
-  const bool acc_aligned = (L & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.dB_acc) |
-                                              reinterpret_cast<uintptr_t>(p.dC_acc)) & 15) == 0;
-
-  for (int c = n_big - 1; c >= 0; --c) {
-    const int t0 = c * kChunk;
-    const int tl = t0 + lane * kItems;
-
-    if (t0 >= len) {
-      // Padding-only chunk (CTA-uniform: len depends on the batch only).
-      if (active) {
-        float2 zero[kHalf];
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) zero[i] = make_float2(0.f, 0.f);
-        store_run2(du_row, tl, L, zero);
-        store_run2(ddl_row, tl, L, zero);
-        if (dz_row) store_run2(dz_row, tl, L, zero);
-      }
-      continue;
-    }
-
-    // ---- stage this chunk's u, delta, dout, z and pre-gate runs
-    const int ycoord = c * (kChunk / kItems);
-    if (use_tma) {
-      if (threadIdx.x == 0) {
-        bulk_wait_read_all();  // the previous chunk's du/ddelta stores left smem
-        fence_proxy_async_smem();  // and the CTA's reads of those buffers are done
-        const uint32_t blk = Sh::kArr * sizeof(T);
-        mbar_arrive_expect_tx(&sh.bar[2], (z_row ? 5u : 3u) * blk);
-        tma_load_3d(&sh.arrU[0][0][0], &maps.u, 0, ycoord, row0, &sh.bar[2]);
-        tma_load_3d(&sh.arrD[0][0][0], &maps.d, 0, ycoord, row0, &sh.bar[2]);
-        tma_load_3d(&sh.zone(1)[0][0][0], &maps.dout, 0, ycoord, row0, &sh.bar[2]);
-        if (z_row) {
-          tma_load_3d(&sh.zone(0)[0][0][0], &maps.z, 0, ycoord, row0, &sh.bar[2]);
-          tma_load_3d(&sh.zone(2)[0][0][0], &maps.pre, 0, ycoord, row0, &sh.bar[2]);
-        }
-      }
-      const bool ok = mbar_wait_bounded(&sh.bar[2], (c_first - c) & 1);
-      if (__syncthreads_or(!ok)) {
-        if (threadIdx.x == 0) {
-          atomicOr(&g_bwd_device_error, kErrTmaTimeout);
-          mbar_wait_bounded(&sh.bar[(c_first - c) * NS & 1], (((c_first - c) * NS) >> 1) & 1);
-          bulk_wait_all();
-        }
-        return;
-      }
-    } else {
-      float2 v[kHalf];
-      load_run2(u_row, tl, lim, v);
-      sts_run16(sh.arrU[warp], lane, v);
-      load_run2(dl_row, tl, lim, v);
-      sts_run16(sh.arrD[warp], lane, v);
-      load_run2(dout_row, tl, lim, v);
-      sts_run16(sh.zone(1)[warp], lane, v);
-      if (z_row) {
-        load_run2(z_row, tl, lim, v);
-        sts_run16(sh.zone(0)[warp], lane, v);
-        load_run2(static_cast<const T*>(p.out_pre) + row * L, tl, lim, v);
-        sts_run16(sh.zone(2)[warp], lane, v);
-      }
-      __syncwarp();
-    }
-
-    // ---- per-step inputs of this lane's run; dz (independent of the scan)
-    float2 dl[kHalf], duv[kHalf], dy[kHalf];
-    float ssum, ssum1;  // sum of delta over the run, and without its first step
-    {
-      float2 uv[kHalf];
-      lds_run16(sh.arrU[warp], lane, uv);
-      lds_run16(sh.arrD[warp], lane, dl);
-      lds_run16(sh.zone(1)[warp], lane, dy);
-      if (z_row) {
-        // dz = dout * (y + D u) * silu'(z), with y + D u saved by the forward
-        float2 zv[kHalf], pv[kHalf], dzv[kHalf];
-        lds_run16(sh.zone(0)[warp], lane, zv);
-        lds_run16(sh.zone(2)[warp], lane, pv);
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) {
-          const float s0 = sigmoid_f(zv[i].x), s1 = sigmoid_f(zv[i].y);
-          const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
-          dzv[i].x = v0 ? dy[i].x * pv[i].x * s0 * fmaf(zv[i].x, 1.f - s0, 1.f) : 0.f;
-          dzv[i].y = v1 ? dy[i].y * pv[i].y * s1 * fmaf(zv[i].y, 1.f - s1, 1.f) : 0.f;
-          dy[i].x *= zv[i].x * s0;
-          dy[i].y *= zv[i].y * s1;
-        }
-        if (tma_store) {
-          sts_run16(sh.zone(2)[warp], lane, dzv);
-        } else if (active) {
-          store_run2(dz_row, tl, L, dzv);
-        }
-      }
-      ssum = 0.f;
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) {
-        const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
-        float x0 = dl[i].x + bias, x1 = dl[i].y + bias;
-        if (p.delta_softplus) {
-          x0 = softplus_f(x0);
-          x1 = softplus_f(x1);
-        }
-        dl[i].x = v0 ? x0 : 0.f;
-        dl[i].y = v1 ? x1 : 0.f;
-        uv[i].x = v0 ? uv[i].x : 0.f;
-        uv[i].y = v1 ? uv[i].y : 0.f;
-        dy[i].x = v0 ? dy[i].x : 0.f;
-        dy[i].y = v1 ? dy[i].y : 0.f;
-        ssum += dl[i].x + dl[i].y;
-        duv[i] = kZOH ? uv[i] : mul2(dl[i], uv[i]);
-      }
-      ssum1 = ssum - dl[0].x;
-    }
-    if (lane < NS) {
-      sh.Aw[warp][lane] = __ldg(p.A + dc * NS + lane);
-      float hsv = 0.f;
-      if (active) {
-        if (c == 0)
-          hsv = p.h0 ? __ldg(p.h0 + row * NS + lane) : 0.f;
-        else
-          hsv = p.chunk_states[(row * p.n_chunks + c * (kChunk / kCkpt) - 1) * NS + lane];
-      }
-      sh.hsw[warp][lane] = hsv;
-    }
-    __syncwarp();
-    if (z_row && tma_store) {
-      fence_proxy_async_smem();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        tma_store_3d(&maps.dz, 0, ycoord, row0, &sh.zone(2)[0][0][0]);
-        bulk_commit();
-      }
-    }
-
-    float2 gA[kHalf], gB[kHalf];
-#pragma unroll
-    for (int i = 0; i < kHalf; ++i) {
-      gA[i] = make_float2(0.f, 0.f);  // sum_n g a h_{t-1} A_n  (ZOH: + g a B u)
-      gB[i] = make_float2(0.f, 0.f);  // sum_n g B_n            (ZOH: g b_bar)
-    }
-
-#pragma unroll 1
-    for (int n = 0; n < NS; ++n) {
-      const int seq = (c_first - c) * NS + n;  // position in the TMA pipeline
-      const int sb = seq & 1;
-      if (use_tma) {
-        if (threadIdx.x == 0) {
-          const int nn = n + 1 < NS ? n + 1 : 0;
-          const int cn = n + 1 < NS ? c : c - 1;
-          if (cn >= 0) {
-            fence_proxy_async_smem();  // readers of that buffer passed a barrier
-            issue(cn, nn, seq + 1);
-          }
-        }
-        const bool ok = mbar_wait_bounded(&sh.bar[sb], (seq >> 1) & 1);
-        if (__syncthreads_or(!ok)) {
-          if (threadIdx.x == 0) {
-            atomicOr(&g_bwd_device_error, kErrTmaTimeout);
-            mbar_wait_bounded(&sh.bar[sb ^ 1], ((seq + 1) >> 1) & 1);
-          }
-          return;
-        }
-      }
-      const float An = sh.Aw[warp][n];
-      const float2 a2 = dup2(An * kLog2e);
-      const float2 A2 = dup2(An);
-      const float hs = sh.hsw[warp][n];
-      float4* tileB = &sh.wrow[sb][warp][0][0];
-      float4* tileC = &sh.wrow[sb][warp][1][0];
-      if (!use_tma) {
-        // stage this state's B/C rows with plain loads, in the TMA's layout
-        stage_bc_plain(sh.bufB[sb], sh.bufC[sb], B_b + static_cast<size_t>(n) * L,
-                       C_b + static_cast<size_t>(n) * L, t0, len);
-        __syncthreads();
-      }
-      const T(*bB)[kItems] = sh.bufB[sb];
-      const T(*bC)[kItems] = sh.bufC[sb];
-
-      // ---- forward recompute: a_t, and h_t for every step of the run
-      float2 ab[kHalf], hv[kHalf];
-      {
-        float H = 0.f;
-#pragma unroll
-        for (int j = 0; j < kHalf / 2; ++j) {
-          float2 Bq[2];
-          lds_quad(bB, lane, j, Bq);
-#pragma unroll
-          for (int ii = 0; ii < 2; ++ii) {
-            const int i = 2 * j + ii;
-            const float2 arg = mul2(dl[i], a2);
-            ab[i] = make_float2(ex2(arg.x), ex2(arg.y));
-            float2 bu;
-            if constexpr (kZOH) {
-              const float inv = 1.f / An;
-              bu.x = Bq[ii].x * (expm1f(dl[i].x * An) * inv) * duv[i].x;
-              bu.y = Bq[ii].y * (expm1f(dl[i].y * An) * inv) * duv[i].y;
-            } else {
-              bu = mul2(Bq[ii], duv[i]);
-            }
-            hv[i] = bu;  // b_t for now; h_t after the re-walk
-            H = fmaf(ab[i].x, H, bu.x);
-            H = fmaf(ab[i].y, H, bu.y);
-          }
-        }
-        float P = ex2(a2.x * ssum);
-        warp_scan_fwd(P, H, lane);
-        float Pe = __shfl_up_sync(0xffffffffu, P, 1);
-        float He = __shfl_up_sync(0xffffffffu, H, 1);
-        if (lane == 0) {
-          Pe = 1.f;
-          He = 0.f;
-        }
-        float h = fmaf(Pe, hs, He);  // h entering this lane's run
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) {
-          hv[i].x = h = fmaf(ab[i].x, h, hv[i].x);
-          hv[i].y = h = fmaf(ab[i].y, h, hv[i].y);
-        }
-      }
-
-      // ---- dC = dy h, written to this warp's row; local adjoint fold
-      float an_last = __shfl_down_sync(0xffffffffu, ab[0].x, 1);
-      if (lane == 31) an_last = 1.f;  // the carry already holds a_{t+1} g_{t+1}
-      float Gr = 0.f;
-      float2 ev[kHalf];  // e_t = dy_t C_t, kept for the re-walk
-#pragma unroll
-      for (int j = kHalf / 2 - 1; j >= 0; --j) {
-        float2 Cq[2];
-        lds_quad(bC, lane, j, Cq);
-        const float2 c0 = mul2(dy[2 * j], hv[2 * j]);
-        const float2 c1 = mul2(dy[2 * j + 1], hv[2 * j + 1]);
-        tileC[tile_slot(lane * (kItems / 4) + j)] = make_float4(c0.x, c0.y, c1.x, c1.y);
-#pragma unroll
-        for (int ii = 1; ii >= 0; --ii) {
-          const int i = 2 * j + ii;
-          const float2 e = mul2(dy[i], Cq[ii]);  // e_t = dy_t C_t
-          ev[i] = e;
-          Gr = fmaf(i == kHalf - 1 ? 0.f : ab[i + 1].x, Gr, e.y);
-          Gr = fmaf(ab[i].y, Gr, e.x);
-        }
-      }
-
-      // ---- adjoint scan: g_t = e_t + a_{t+1} g_{t+1}
-      float g;
-      {
-        // lane map g_next -> Pr g_next + Gr with Pr = a_1 ... a_15 a_next
-        float Pr = ex2(a2.x * ssum1) * an_last;
-        warp_scan_rev(Pr, Gr, lane);
-        float Pe = __shfl_down_sync(0xffffffffu, Pr, 1);
-        float Ge = __shfl_down_sync(0xffffffffu, Gr, 1);
-        if (lane == 31) {
-          Pe = 1.f;
-          Ge = 0.f;
-        }
-        g = fmaf(Pe, sh.gcarry[warp][n], Ge);  // g of the next lane's first step
-      }
-
-      // ---- re-walk g backwards and form the gradient terms
-      float2 dAl = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int j = kHalf / 2 - 1; j >= 0; --j) {
-        float2 Bq[2], dbp[2];
-        lds_quad(bB, lane, j, Bq);
-#pragma unroll
-        for (int ii = 1; ii >= 0; --ii) {
-          const int i = 2 * j + ii;
-          const float2 e = ev[i];
-          float2 gv;
-          gv.y = g = fmaf(i == kHalf - 1 ? an_last : ab[i + 1].x, g, e.y);
-          gv.x = g = fmaf(ab[i].y, g, e.x);
-          float2 bu, bb;
-          if constexpr (kZOH) {
-            const float inv = 1.f / An;
-            bb.x = expm1f(dl[i].x * An) * inv;
-            bb.y = expm1f(dl[i].y * An) * inv;
-            bu = mul2(mul2(Bq[ii], bb), duv[i]);
-          } else {
-            bu = mul2(Bq[ii], duv[i]);
-          }
-          // a_t h_{t-1} = h_t - b_t
-          const float2 ah = add2(hv[i], make_float2(-bu.x, -bu.y));
-          const float2 w = mul2(gv, ah);
-          gA[i] = fma2(w, A2, gA[i]);
-          dAl = fma2(w, dl[i], dAl);
-          if constexpr (kZOH) {
-            // d b_t/d delta = a_t B u, d b_t/d A = B u (delta a_t - b_bar) / A
-            const float2 gBu = mul2(gv, mul2(Bq[ii], duv[i]));
-            gA[i] = fma2(gBu, ab[i], gA[i]);
-            const float inv = 1.f / An;
-            dAl.x += gBu.x * (dl[i].x * ab[i].x - bb.x) * inv;
-            dAl.y += gBu.y * (dl[i].y * ab[i].y - bb.y) * inv;
-            gB[i] = fma2(gv, mul2(Bq[ii], bb), gB[i]);
-            dbp[ii] = mul2(gv, mul2(bb, duv[i]));
-          } else {
-            gB[i] = fma2(gv, Bq[ii], gB[i]);
-            dbp[ii] = mul2(gv, duv[i]);
-          }
-        }
-        tileB[tile_slot(lane * (kItems / 4) + j)] =
-            make_float4(dbp[0].x, dbp[0].y, dbp[1].x, dbp[1].y);
-      }
-      const float gnext = __shfl_sync(0xffffffffu, ab[0].x * g, 0);
-      if (lane == 0) sh.gcarry[warp][n] = gnext;
-      sh.dA[warp][n][lane] += dAl.x + dAl.y;
-      if (n == 0 && threadIdx.x == 0 && z_row && tma_store)
-        bulk_wait_read_all();  // dz left the zone before wrow[1] is written
-      __syncthreads();
-
-      // ---- add the warps' dB/dC rows of this state into the fp32 accumulators
-      {
-        const size_t base = (static_cast<size_t>(b) * NS + n) * L;
-        const bool whole = t0 + kChunk <= len;  // CTA-uniform
-#pragma unroll
-        for (int k = 0; k < kFlushPerThread; ++k) {
-          const int q = threadIdx.x + k * kBwdWarps * 32;
-          const int which = q / (kChunk / 4);  // 0: dB, 1: dC
-          const int qq = q % (kChunk / 4);
-          const float4* src = &sh.wrow[sb][0][which][flush_slot[k]];
-          float4 v0 = src[0];
-          float2 lo = make_float2(v0.x, v0.y), hi = make_float2(v0.z, v0.w);
-#pragma unroll
-          for (int w = 1; w < kBwdWarps; ++w) {
-            const float4 x = src[w * 2 * (kChunk / 4)];
-            lo = add2(lo, make_float2(x.x, x.y));
-            hi = add2(hi, make_float2(x.z, x.w));
-          }
-          const float4 v = make_float4(lo.x, lo.y, hi.x, hi.y);
-          float* gp = (which ? p.dC_acc : p.dB_acc) + base + t0 + qq * 4;
-          const int t = t0 + qq * 4;
-          if (whole && acc_aligned) {
-            atomicAdd(reinterpret_cast<float4*>(gp), v);
-          } else if (t < len) {
-            const float e4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (t + e < len) atomicAdd(gp + e, e4[e]);
-          }
-        }
-      }
-    }
-
-    // ---- per-step epilogue: du, ddelta (dz was written before the scan)
-    {
-      float2 uv[kHalf];
-      lds_run16(sh.arrU[warp], lane, uv);
-      float2 o_du[kHalf], o_dd[kHalf];
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) {
-        const bool v0 = tl + 2 * i < lim, v1 = tl + 2 * i + 1 < lim;
-        uv[i].x = v0 ? uv[i].x : 0.f;
-        uv[i].y = v1 ? uv[i].y : 0.f;
-        // ddelta_eff = sum_n g (B u + a h_{t-1} A)   (Euler; ZOH: gA holds all)
-        float2 gd = kZOH ? gA[i] : fma2(uv[i], gB[i], gA[i]);
-        if (p.delta_softplus) {
-          // d softplus(x)/dx = sigmoid(x) = 1 - e^{-softplus(x)}
-          gd.x *= sigmoid_from_softplus(dl[i].x);
-          gd.y *= sigmoid_from_softplus(dl[i].y);
-        }
-        const float2 gu = kZOH ? gB[i] : mul2(dl[i], gB[i]);
-        float2 du_ = fma2(dup2(Dv), dy[i], gu);
-        gd.x = v0 ? gd.x : 0.f;
-        gd.y = v1 ? gd.y : 0.f;
-        du_.x = v0 ? du_.x : 0.f;
-        du_.y = v1 ? du_.y : 0.f;
-        o_dd[i] = gd;
-        o_du[i] = du_;
-        dD_acc = fmaf(dy[i].x, uv[i].x, fmaf(dy[i].y, uv[i].y, dD_acc));
-        dbias_acc += gd.x + gd.y;
-      }
-      if (tma_store) {
-        sts_run16(sh.arrU[warp], lane, o_du);
-        sts_run16(sh.arrD[warp], lane, o_dd);
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-          tma_store_3d(&maps.du, 0, ycoord, row0, &sh.arrU[0][0][0]);
-          tma_store_3d(&maps.dd, 0, ycoord, row0, &sh.arrD[0][0][0]);
-          bulk_commit();
-        }
-      } else {
-        if (active) {
-          store_run2(du_row, tl, L, o_du);
-          store_run2(ddl_row, tl, L, o_dd);
-        }
-        __syncthreads();  // arrU/arrD are refilled by the next chunk
-      }
-    }
-  }
-  if (use_tma && threadIdx.x == 0) bulk_wait_all();
-
-  // ---- per-row results
-  dD_acc = warp_sum(dD_acc);
-  dbias_acc = warp_sum(dbias_acc);
-  float dAv[NS];
-#pragma unroll
-  for (int n = 0; n < NS; ++n) dAv[n] = warp_sum(sh.dA[warp][n][lane]);
-  if (active && lane == 0) {
-#pragma unroll
-    for (int n = 0; n < NS; ++n) {
-      p.dA_part[row * NS + n] = dAv[n];
-      if (p.dh0) p.dh0[row * NS + n] = sh.gcarry[warp][n];
-    }
-    p.dD_part[row] = dD_acc;
-    p.dbias_part[row] = dbias_acc;
-  }
-}
-
 // ============================================================================
-// Tile backward (the default): sequential in time inside each lane.
+// Tile backward: sequential in time inside each lane.
 //
 // A lane owns kS states of one channel, kLPC = NS / kS lanes a channel, and a
 // one-warp CTA kCh = 32 / kLPC channels of one batch (the forward's
-// decomposition). The forward saves the state at the end of every kBT-step
-// tile, so tiles are independent given their entering state. The CTA walks
-// the tiles in reverse; per tile
+// decomposition). The forward saves the state after every kGrp = 4 steps,
+// so groups are independent given their entering state. The CTA walks
+// kBT-step tiles in reverse; per tile
 //   0. TMA stages delta, u, dout, z, pre-gate ([kCh channels x kBT steps])
 //      and B, C ([N x kBT]) with the 128-byte (fp32) / 64-byte (bf16)
 //      swizzle; the next tile's copies fly while this one computes;
 //   1. transform: delta_eff = softplus(delta + bias) and dy = dout silu(z)
 //      become fp32 work rows (for fp32 I/O in place of delta and dout), and
 //      dz = dout pre silu'(z) is written in place of z;
-//   2. forward pass over the tile from its saved state, keeping the state at
-//      the start of each kGrp-step group in registers;
+//   2. the saved state entering each group is loaded into registers;
 //   3. groups in reverse: recompute a_t, h_t over the group, run the adjoint
 //      g_t = dy_t C_t + a_{t+1} g_{t+1} per state, and form per step
 //      sum_n g B and sum_n g A a h_{t-1} (summed over the channel's lanes,
@@ -662,8 +47,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
 // Shared memory is kept under 20 KB per CTA (fp32, N = 16) so that a
 // Mamba-130M layer's CTAs are all resident at once (11 per SM).
 // ============================================================================
-constexpr int kBT = kCkpt;      // steps per tile (one saved carry per tile)
-constexpr int kGrp = 4;         // steps per group
+constexpr int kBT = 32;         // steps per tile
+constexpr int kGrp = kCkpt;     // steps per group (one saved carry per group)
 constexpr int kNG = kBT / kGrp;  // groups per tile
 
 template <int NS>
@@ -946,19 +331,35 @@ __global__ void __launch_bounds__(32)
     float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
     float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
 
-    // state entering the tile
-    float h_in[kS];
+    // ---- 2. the saved state entering each group (groups starting at or
+    // past the valid length carry delta = 0 and only need a finite state)
+    // Loaded here, used (and, for N = 16, permuted) only when the group
+    // is processed, so the loads' latency hides behind the transform.
+    float hck[kNG][kS];
 #pragma unroll
-    for (int j = 0; j < kS; ++j) {
-      const int n = st_of(j);
-      float v = 0.f;
-      if (act) {
-        if (k > 0)
-          v = p.chunk_states[(row * p.n_chunks + k - 1) * NS + n];
-        else if (p.h0)
-          v = __ldg(p.h0 + row * NS + n);
+    for (int g = 0; g < kNG; ++g) {
+      const int gi = t0 / kCkpt + g;  // carry index of the group
+      const bool live = act && t0 + g * kGrp < len;
+      if (live && gi > 0) {
+        // the forward's lane q kept state q + kLPC j' at slot j'
+        const float* cs =
+            p.chunk_states + carry_offset(b, gi - 1, p.n_chunks, p.dim, d, NS) + q * kS;
+        if constexpr (kS == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(cs);
+          hck[g][0] = v.x;
+          hck[g][1] = v.y;
+          hck[g][2] = v.z;
+          hck[g][3] = v.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < kS; ++j) hck[g][j] = cs[j];
+        }
+      } else {
+        // forward slot order here too (h0 is in natural state order)
+#pragma unroll
+        for (int j = 0; j < kS; ++j)
+          hck[g][j] = (live && p.h0) ? __ldg(p.h0 + row * NS + q + kLPC * j) : 0.f;
       }
-      h_in[j] = v;
     }
 
     if (use_tma) {
@@ -1059,44 +460,6 @@ __global__ void __launch_bounds__(32)
       }
     };
 
-    // ---- 2. forward over the tile: the state entering each group
-    float hck[kNG][kS];
-    {
-      float h[kS];
-#pragma unroll
-      for (int j = 0; j < kS; ++j) h[j] = h_in[j];
-#pragma unroll
-      for (int g = 0; g < kNG; ++g) {
-#pragma unroll
-        for (int j = 0; j < kS; ++j) hck[g][j] = h[j];
-        if (g == kNG - 1) break;
-        const int tg = g * kGrp;
-        float2 dlp[2], dup_[2];
-        load_dl_du(tg, dlp, dup_);
-#pragma unroll
-        for (int j = 0; j < kS; ++j) {
-          const float4 B4 = ld4s(bB, st_of(j), tg);
-          const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
-          const float2 a2p = dup2(a2[j]);
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float2 arg = mul2(dlp[e], a2p);
-            const float2 ab = make_float2(ex2(arg.x), ex2(arg.y));
-            float2 bu;
-            if constexpr (kZOH) {
-              const float inv = 1.f / Av[j];
-              bu.x = Bp[e].x * (expm1f(dlp[e].x * Av[j]) * inv) * dup_[e].x;
-              bu.y = Bp[e].y * (expm1f(dlp[e].y * Av[j]) * inv) * dup_[e].y;
-            } else {
-              bu = mul2(Bp[e], dup_[e]);
-            }
-            h[j] = fmaf(ab.x, h[j], bu.x);
-            h[j] = fmaf(ab.y, h[j], bu.y);
-          }
-        }
-      }
-    }
-
     // ---- 3. groups in reverse
 #pragma unroll
     for (int g = kNG - 1; g >= 0; --g) {
@@ -1116,9 +479,18 @@ __global__ void __launch_bounds__(32)
         const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
         const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
         const float2 a2p = dup2(a2[j]);
-        // recompute a_t and h_t over the group
+        // recompute a_t and h_t over the group (this lane's slot j is the
+        // forward's slot j ^ perm)
         float2 ab[2], hv[2], bu[2], bb[2];
-        float hh = hck[g][j];
+        float hh;
+        if constexpr (kShflFlush) {
+          const int sl = j ^ perm;
+          const float lo = (sl & 1) ? hck[g][1] : hck[g][0];
+          const float hi = (sl & 1) ? hck[g][3] : hck[g][2];
+          hh = (sl & 2) ? hi : lo;
+        } else {
+          hh = hck[g][j];
+        }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float2 arg = mul2(dlp[e], a2p);
@@ -1342,51 +714,6 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src,
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-template <int NS, typename T, bool kZOH>
-static cudaError_t launch_bwd_t(const BwdParams& p, const BwdMaps& maps,
-                                cudaStream_t stream) {
-  const size_t smem = sizeof(BwdShared<NS, T>);
-  auto kern = ss_bwd_kernel<NS, T, kZOH>;
-  cudaError_t e = cudaFuncSetAttribute(
-      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  dim3 grid((p.dim + kBwdWarps - 1) / kBwdWarps, p.batch);
-  kern<<<grid, kBwdWarps * 32, smem, stream>>>(p, maps);
-  return cudaPeekAtLastError();
-}
-
-template <typename T, bool kZOH>
-static cudaError_t launch_bwd_n(const BwdParams& p, const BwdMaps& maps, int dstate,
-                                cudaStream_t stream) {
-  switch (dstate) {
-    case 1: return launch_bwd_t<1, T, kZOH>(p, maps, stream);
-    case 2: return launch_bwd_t<2, T, kZOH>(p, maps, stream);
-    case 4: return launch_bwd_t<4, T, kZOH>(p, maps, stream);
-    case 8: return launch_bwd_t<8, T, kZOH>(p, maps, stream);
-    case 16: return launch_bwd_t<16, T, kZOH>(p, maps, stream);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
-// A (rows x L) operand as a 3-D tensor [rows][L/kItems][kItems], in boxes of
-// box_rows rows x 32 runs x kItems steps, swizzled so that each lane's run is
-// a conflict-free 16-byte-chunk read (64-byte swizzle for fp32 runs, 32-byte
-// for bf16).
-static bool encode_runs(CUtensorMap* m, const void* base, int io_dtype, uint64_t rows,
-                        uint64_t L, uint32_t box_rows) {
-  auto fn = tensor_map_encoder();
-  if (!fn) return false;
-  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kItems), L / kItems, rows};
-  const cuuint64_t strides[2] = {kItems * esize, L * esize};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kItems), 32, box_rows};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(m, io_dtype == MSS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-            3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            io_dtype == MSS_BF16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 static cudaError_t launch_bwd_finish(const BwdParams& p, int dstate, int io_dtype,
                                      void* dB_out, void* dC_out, float* dA, float* dD,
                                      float* ddelta_bias, cudaStream_t stream);
@@ -1480,11 +807,6 @@ static cudaError_t launch_bwd_tile(const BwdParams& p, int dstate, int io_dtype,
              : launch_bwd_tile_n<float, false>(pk, maps, dstate, stream);
 }
 
-static bool use_chunk_kernel() {
-  const char* v = getenv("MAMBA_SS_BWD_KERNEL");
-  return v && strcmp(v, "chunk") == 0;
-}
-
 cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream) {
@@ -1494,48 +816,13 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
   e = cudaMemsetAsync(p.dC_acc, 0, n_bnl * sizeof(float), stream);
   if (e != cudaSuccess) return e;
 
-  if (!use_chunk_kernel()) {
-    e = launch_bwd_tile(p, dstate, io_dtype, zoh, stream);
-    if (e != cudaSuccess) return e;
-    return launch_bwd_finish(p, dstate, io_dtype, dB_out, dC_out, dA, dD, ddelta_bias, stream);
-  }
-
-  BwdParams pk = p;
-  BwdMaps maps;
-  memset(&maps, 0, sizeof(maps));
-  const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
-  const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  pk.tma_ok = p.seqlen % kItems == 0 && (p.seqlen * esize) % 16 == 0 && al16(p.B) &&
-              al16(p.C) && al16(p.u) && al16(p.delta) && al16(p.dout) && al16(p.du) &&
-              al16(p.ddelta) && (!p.z || (al16(p.z) && al16(p.dz) && al16(p.out_pre)));
-  if (pk.tma_ok) {
-    const uint64_t brows = static_cast<uint64_t>(p.batch) * dstate;
-    const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
-    const uint64_t L = p.seqlen;
-    pk.tma_ok = encode_runs(&maps.b, p.B, io_dtype, brows, L, 1) &&
-                encode_runs(&maps.c, p.C, io_dtype, brows, L, 1) &&
-                encode_runs(&maps.u, p.u, io_dtype, rows, L, kBwdWarps) &&
-                encode_runs(&maps.d, p.delta, io_dtype, rows, L, kBwdWarps) &&
-                encode_runs(&maps.dout, p.dout, io_dtype, rows, L, kBwdWarps) &&
-                encode_runs(&maps.du, p.du, io_dtype, rows, L, kBwdWarps) &&
-                encode_runs(&maps.dd, p.ddelta, io_dtype, rows, L, kBwdWarps) &&
-                (!p.z || (encode_runs(&maps.z, p.z, io_dtype, rows, L, kBwdWarps) &&
-                          encode_runs(&maps.pre, p.out_pre, io_dtype, rows, L, kBwdWarps) &&
-                          encode_runs(&maps.dz, p.dz, io_dtype, rows, L, kBwdWarps)));
-  }
-  if (io_dtype == MSS_BF16) {
-    e = zoh ? launch_bwd_n<__nv_bfloat16, true>(pk, maps, dstate, stream)
-            : launch_bwd_n<__nv_bfloat16, false>(pk, maps, dstate, stream);
-  } else {
-    e = zoh ? launch_bwd_n<float, true>(pk, maps, dstate, stream)
-            : launch_bwd_n<float, false>(pk, maps, dstate, stream);
-  }
+  e = launch_bwd_tile(p, dstate, io_dtype, zoh, stream);
   if (e != cudaSuccess) return e;
   return launch_bwd_finish(p, dstate, io_dtype, dB_out, dC_out, dA, dD, ddelta_bias, stream);
 }
 
 // The batch reduction of the parameter gradients and (bf16 I/O) the
-// fp32 -> bf16 conversion of dB/dC, after either backward kernel.
+// fp32 -> bf16 conversion of dB/dC, after the scan kernel.
 static cudaError_t launch_bwd_finish(const BwdParams& p, int dstate, int io_dtype,
                                      void* dB_out, void* dC_out, float* dA, float* dD,
                                      float* ddelta_bias, cudaStream_t stream) {

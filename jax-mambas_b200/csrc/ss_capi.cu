@@ -120,6 +120,8 @@ mss_status mamba_ss_fused_fwd(
     return fail(MSS_INVALID_ARGUMENT,
                 "mamba_ss_fused_fwd: u, delta, A, B, C, out and chunk_states "
                 "must be non-null");
+  if (reinterpret_cast<uintptr_t>(chunk_states) & 15)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_fwd: chunk_states must be 16-byte aligned");
   mss::FwdParams p{};
   p.batch = batch;
   p.dim = dim;
@@ -164,6 +166,8 @@ mss_status mamba_ss_fused_bwd(
     return fail(MSS_INVALID_ARGUMENT,
                 "mamba_ss_fused_bwd: u, delta, A, B, C, chunk_states, dout, du, "
                 "ddelta, dA, dB and dC must be non-null");
+  if (reinterpret_cast<uintptr_t>(chunk_states) & 15)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_bwd: chunk_states must be 16-byte aligned");
   if (z && (!dz || !out_pre))
     return fail(MSS_INVALID_ARGUMENT,
                 "mamba_ss_fused_bwd: z given without dz or out_pre");

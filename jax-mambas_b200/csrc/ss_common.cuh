@@ -1,15 +1,10 @@
-// Shared device code of the sm_100a selective scan: parameter blocks, typed
-// row loads/stores and the per-element activation helpers.
+// Shared device code of the sm_100a selective scan: parameter blocks,
+// activation helpers, TMA / mbarrier wrappers and packed fp32 pairs.
 //
-// Work decomposition (forward and backward):
-//   * one warp owns one (batch, channel) row and walks L in chunks of
-//     MSS_CHUNK = 32 lanes x kItems steps;
-//   * lane i owns the kItems consecutive steps [t0 + i*kItems, ...) of a chunk;
-//   * the recurrence h_t = a_t h_{t-1} + b_t runs per state in fp32 registers:
-//     a lane-local pass, a warp-shuffle scan of the (prod a, h) pairs over the
-//     32 lanes, then a lane-local re-scan seeded with the lane's prefix;
-//   * the carry across chunks is kept per state in registers (forward) or in
-//     shared memory (backward).
+// Work decomposition (forward and backward): the recurrence
+// h_t = a_t h_{t-1} + b_t runs sequentially in time inside each lane; a lane
+// owns up to 4 states of one channel, and the forward saves the state after
+// every MSS_CHUNK (4) steps so that the backward can restart anywhere.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -21,10 +16,17 @@
 
 namespace mss {
 
-constexpr int kItems = 16;                  // steps per lane per chunk
-constexpr int kChunk = 32 * kItems;         // steps per chunk of the warp-scan backward
-constexpr int kCkpt = MSS_CHUNK;            // steps per saved carry (chunk_states entry)
-static_assert(kChunk % kCkpt == 0, "a chunk ends on a saved carry");
+constexpr int kCkpt = MSS_CHUNK;  // steps per saved carry (chunk_states entry)
+
+// Saved carries are (batch, n_chunks, dim, dstate) fp32, time-major so that a
+// warp's stores and loads of one carry index are contiguous. Inside a
+// (batch, index, channel) entry the states are in lane order: the lane that
+// owns states q, q + lpc, q + 2 lpc, ... (lpc lanes per channel) keeps them
+// at q * (dstate / lpc) + 0, 1, 2, ..., one 16-byte word for 4 states.
+__device__ __forceinline__ size_t carry_offset(int b, int idx, int n_chunks, int dim, int d,
+                                               int dstate) {
+  return ((static_cast<size_t>(b) * n_chunks + idx) * dim + d) * dstate;
+}
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct FwdParams {
@@ -114,95 +116,12 @@ struct Elem<__nv_bfloat16> {
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
 
-// Loads kItems consecutive elements row[t .. t+kItems) as fp32; elements at or
-// beyond `limit` read as 0. Uses 16-byte loads when the run is whole and
-// 16-byte aligned.
-template <typename T>
-__device__ __forceinline__ void load_run(const T* row, int t, int limit,
-                                         float (&v)[kItems]) {
-  const T* p = row + t;
-  const bool whole = t + kItems <= limit;
-  if (whole && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
-    if constexpr (sizeof(T) == 4) {
-      const float4* q = reinterpret_cast<const float4*>(p);
-#pragma unroll
-      for (int j = 0; j < kItems / 4; ++j) {
-        float4 f = __ldg(q + j);
-        v[4 * j + 0] = f.x;
-        v[4 * j + 1] = f.y;
-        v[4 * j + 2] = f.z;
-        v[4 * j + 3] = f.w;
-      }
-    } else {
-      static_assert(kItems % 8 == 0, "bf16 runs load 8 elements per 16 bytes");
-      const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-      for (int j = 0; j < kItems / 8; ++j) {
-        uint4 w = __ldg(q + j);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f = __bfloat1622float2(h[e]);
-          v[8 * j + 2 * e] = f.x;
-          v[8 * j + 2 * e + 1] = f.y;
-        }
-      }
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < kItems; ++k)
-      v[k] = (t + k < limit) ? Elem<T>::ld(p + k) : 0.f;
-  }
-}
-
-// Stores v[0 .. kItems) to row[t ..); elements at or beyond `limit` are not
-// written.
-template <typename T>
-__device__ __forceinline__ void store_run(T* row, int t, int limit,
-                                          const float (&v)[kItems]) {
-  T* p = row + t;
-  const bool whole = t + kItems <= limit;
-  if (whole && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
-    if constexpr (sizeof(T) == 4) {
-      float4* q = reinterpret_cast<float4*>(p);
-#pragma unroll
-      for (int j = 0; j < kItems / 4; ++j)
-        q[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-      uint4* q = reinterpret_cast<uint4*>(p);
-#pragma unroll
-      for (int j = 0; j < kItems / 8; ++j) {
-        uint4 w;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
-        q[j] = w;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < kItems; ++k)
-      if (t + k < limit) Elem<T>::st(p + k, v[k]);
-  }
-}
-
 // ------------------------------------------------------------- activations
 // 2^x on the special-function unit.
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// softplus(x) = log(1 + e^x), the function jax.nn.softplus evaluates
-// (mamba/mamba1.py:76,165); large x pass through unchanged.
-__device__ __forceinline__ float softplus(float x) {
-  return x <= 20.f ? log1pf(expf(x)) : x;
-}
-
-__device__ __forceinline__ float sigmoid(float x) {
-  return 1.f / (1.f + expf(-x));
 }
 
 // log1p(t) for t in [0, 1] from the series
@@ -268,17 +187,6 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// 1-D TMA copy global -> shared of `bytes` (multiple of 16, both addresses
-// 16-byte aligned); completion is counted on `bar`.
-__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // 2-D TMA tile copy global -> shared: the box at column x (innermost, a
 // multiple of 16 bytes) and row y of the tensor map lands densely at dst
 // (128-byte aligned); elements outside the tensor are filled with zeros and
@@ -292,26 +200,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
-// 3-D TMA tile copy global -> shared (coordinates innermost first).
-__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// 3-D TMA tile store shared -> global (elements outside the tensor are not
-// written); completion is tracked by the issuing thread's bulk async-groups.
-__device__ __forceinline__ void tma_store_3d(const void* tmap, int x, int y, int z,
-                                             const void* src) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
-          reinterpret_cast<uint64_t>(tmap)),
-      "r"(x), "r"(y), "r"(z), "r"(smem_u32(src))
-      : "memory");
-}
 // 2-D TMA tile store shared -> global (elements outside the tensor are not
 // written); completion is tracked by the issuing thread's bulk async-groups.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* src) {
@@ -360,35 +248,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // TMA copies (see mamba_ss_take_device_error()).
 constexpr unsigned int kErrTmaTimeout = 1u;
 
-// ------------------------------------------------------------ warp scans
-// Inclusive scan over lanes of the affine maps h -> P h + H, composed left
-// to right: lane i ends with the composition of lanes 0..i.
-__device__ __forceinline__ void warp_scan_fwd(float& P, float& H, int lane) {
-#pragma unroll
-  for (int s = 1; s < 32; s <<= 1) {
-    const float Pp = __shfl_up_sync(0xffffffffu, P, s);
-    const float Hp = __shfl_up_sync(0xffffffffu, H, s);
-    if (lane >= s) {
-      H = fmaf(P, Hp, H);
-      P *= Pp;
-    }
-  }
-}
-
-// Inclusive scan over lanes of the maps g -> P g + G composed right to left:
-// lane i ends with the composition of lanes i..31.
-__device__ __forceinline__ void warp_scan_rev(float& P, float& G, int lane) {
-#pragma unroll
-  for (int s = 1; s < 32; s <<= 1) {
-    const float Pn = __shfl_down_sync(0xffffffffu, P, s);
-    const float Gn = __shfl_down_sync(0xffffffffu, G, s);
-    if (lane + s < 32) {
-      G = fmaf(P, Gn, G);
-      P *= Pn;
-    }
-  }
-}
-
 // ------------------------------------------------------- packed fp32 pairs
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
@@ -396,24 +255,5 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
-
-// Loads a run as kItems/2 pairs (items 2i, 2i+1).
-template <typename T>
-__device__ __forceinline__ void load_run2(const T* row, int t, int limit,
-                                          float2 (&v)[kItems / 2]) {
-  load_run(row, t, limit, reinterpret_cast<float(&)[kItems]>(v));
-}
-
-template <typename T>
-__device__ __forceinline__ void store_run2(T* row, int t, int limit,
-                                           const float2 (&v)[kItems / 2]) {
-  store_run(row, t, limit, reinterpret_cast<const float(&)[kItems]>(v));
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
-  return v;
-}
 
 }  // namespace mss

@@ -23,7 +23,7 @@
 //      kS-state partial sums of C_t h_t are reduced over the channel's lanes;
 //   3. emit: out = (y + D u) * silu(z) and the pre-gate y + D u (read by the
 //      backward for dz) are written coalesced.
-// The state at the end of every tile (MSS_CHUNK steps) is saved for the backward. Rows whose
+// The state after every MSS_CHUNK (4) steps is saved for the backward. Rows whose
 // length or base address is not 16-byte aligned take the same path with the
 // staging done by plain loads instead of TMA.
 #include <cudaTypedefs.h>
@@ -40,7 +40,7 @@ __device__ unsigned int g_fwd_device_error = 0;
 constexpr int kTile = 32;  // steps staged per pass
 constexpr int kPad = 4;    // row padding (floats) of the fp32 work tiles
 constexpr int kRow = kTile + kPad;
-static_assert(kCkpt == kTile, "a carry is saved at the end of every tile");
+static_assert(kTile % kCkpt == 0 && kCkpt == 4, "a carry is saved after every 4 steps");
 
 template <int NS>
 struct FwdCfg {
@@ -346,15 +346,21 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
 #pragma unroll
           for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] += yp[e];
         }
+        // carry after these 4 steps (entries past the valid length are not
+        // written: the backward never reads them)
+        if (lane_active) {
+          float* cs = p.chunk_states + carry_offset(b, (t0 + tt) / kCkpt, p.n_chunks, p.dim, d, NS) +
+                      q * kS;
+          if constexpr (kS == 4) {
+            *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kS; ++j) cs[j] = h[j];
+          }
+        }
       }
     }
 
-    // ---- carry checkpoint at the end of every tile
-    if (lane_active) {
-#pragma unroll
-      for (int j = 0; j < kS; ++j)
-        p.chunk_states[(row * p.n_chunks + k) * NS + q + kLPC * j] = h[j];
-    }
     __syncthreads();
 
     // ---- 3. emit out = (y + D u) * silu(z), and y + D u, 4 steps per item

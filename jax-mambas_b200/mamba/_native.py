@@ -22,7 +22,7 @@ MSS_F32 = 0
 MSS_BF16 = 1
 MSS_EULER = 0
 MSS_ZOH = 1
-CHUNK = 32
+CHUNK = 4
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
