@@ -331,36 +331,37 @@ __global__ void __launch_bounds__(32)
     float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
     float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
 
-    // ---- 2. the saved state entering each group (groups starting at or
-    // past the valid length carry delta = 0 and only need a finite state)
-    // Loaded here, used (and, for N = 16, permuted) only when the group
-    // is processed, so the loads' latency hides behind the transform.
-    float hck[kNG][kS];
-#pragma unroll
-    for (int g = 0; g < kNG; ++g) {
+    // ---- 2. the saved state entering each group, in the forward's slot
+    // order (lane q: state q + kLPC j' at slot j'); groups starting at or
+    // past the valid length carry delta = 0 and only need a finite state.
+    // The walk below prefetches two groups ahead so that the loads' latency
+    // hides behind the work of the groups in between.
+    auto load_carry = [&](int g) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       const int gi = t0 / kCkpt + g;  // carry index of the group
-      const bool live = act && t0 + g * kGrp < len;
-      if (live && gi > 0) {
-        // the forward's lane q kept state q + kLPC j' at slot j'
-        const float* cs =
-            p.chunk_states + carry_offset(b, gi - 1, p.n_chunks, p.dim, d, NS) + q * kS;
-        if constexpr (kS == 4) {
-          const float4 v = *reinterpret_cast<const float4*>(cs);
-          hck[g][0] = v.x;
-          hck[g][1] = v.y;
-          hck[g][2] = v.z;
-          hck[g][3] = v.w;
-        } else {
-#pragma unroll
-          for (int j = 0; j < kS; ++j) hck[g][j] = cs[j];
+      if (act && t0 + g * kGrp < len) {
+        if (gi > 0) {
+          const float* cs =
+              p.chunk_states + carry_offset(b, gi - 1, p.n_chunks, p.dim, d, NS) + q * kS;
+          if constexpr (kS == 4) {
+            v = *reinterpret_cast<const float4*>(cs);
+          } else {
+            v.x = cs[0];
+            if constexpr (kS > 1) v.y = cs[1];
+          }
+        } else if (p.h0) {
+          const float* h0 = p.h0 + row * NS + q;
+          v.x = __ldg(h0);
+          if constexpr (kS > 1) v.y = __ldg(h0 + kLPC);
+          if constexpr (kS > 2) {
+            v.z = __ldg(h0 + 2 * kLPC);
+            v.w = __ldg(h0 + 3 * kLPC);
+          }
         }
-      } else {
-        // forward slot order here too (h0 is in natural state order)
-#pragma unroll
-        for (int j = 0; j < kS; ++j)
-          hck[g][j] = (live && p.h0) ? __ldg(p.h0 + row * NS + q + kLPC * j) : 0.f;
       }
-    }
+      return v;
+    };
+    float4 carry1 = load_carry(kNG - 1), carry2 = load_carry(kNG - 2);
 
     if (use_tma) {
       bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
@@ -461,9 +462,12 @@ __global__ void __launch_bounds__(32)
     };
 
     // ---- 3. groups in reverse
-#pragma unroll
+#pragma unroll 1
     for (int g = kNG - 1; g >= 0; --g) {
       const int tg = g * kGrp;
+      const float4 hcur = carry1;
+      carry1 = carry2;
+      if (g >= 2) carry2 = load_carry(g - 2);
       float2 dlp[2], dup_[2];
       load_dl_du(tg, dlp, dup_);
       const float4 dy4 = ld4s(wY, c, tg);
@@ -483,13 +487,11 @@ __global__ void __launch_bounds__(32)
         // forward's slot j ^ perm)
         float2 ab[2], hv[2], bu[2], bb[2];
         float hh;
-        if constexpr (kShflFlush) {
+        {
           const int sl = j ^ perm;
-          const float lo = (sl & 1) ? hck[g][1] : hck[g][0];
-          const float hi = (sl & 1) ? hck[g][3] : hck[g][2];
+          const float lo = (sl & 1) ? hcur.y : hcur.x;
+          const float hi = (sl & 1) ? hcur.w : hcur.z;
           hh = (sl & 2) ? hi : lo;
-        } else {
-          hh = hck[g][j];
         }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
