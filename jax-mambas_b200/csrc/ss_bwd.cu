@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(32)
     };
 
     // ---- 3. groups in reverse
-#pragma unroll 1
+#pragma unroll 2
     for (int g = kNG - 1; g >= 0; --g) {
       const int tg = g * kGrp;
       const float4 hcur = carry1;
