@@ -100,6 +100,25 @@ __device__ __forceinline__ int sw_idx(const __nv_bfloat16*, int r, int t) {
   return r * kBT + ((((t >> 3) ^ ((r >> 1) & 3)) << 3) | (t & 7));
 }
 
+// The same addressing split into a per-row part (row pointer, swizzle key,
+// computed once per tile) and a per-group part: group g's steps 4g .. 4g+3
+// of a row start grp_off(row key, g) elements after the row pointer.
+__device__ __forceinline__ int row_key(const float*, int r) { return r & 7; }
+__device__ __forceinline__ int row_key(const __nv_bfloat16*, int r) { return (r >> 1) & 3; }
+__device__ __forceinline__ int grp_off(const float*, int key, int g) { return (g ^ key) << 2; }
+__device__ __forceinline__ int grp_off(const __nv_bfloat16*, int key, int g) {
+  return (((g >> 1) ^ key) << 3) | ((g & 1) << 2);
+}
+__device__ __forceinline__ float4 ld4p(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+__device__ __forceinline__ float4 ld4p(const __nv_bfloat16* p) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // Steps t .. t+3 (t a multiple of 4) of row r as fp32.
 __device__ __forceinline__ float4 ld4s(const float* tile, int r, int t) {
   return *reinterpret_cast<const float4*>(tile + sw_idx(tile, r, t));
@@ -167,14 +186,6 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, bool vec
   }
 }
 
-// acc += the partner lane's (lane ^ m) v, component-wise.
-__device__ __forceinline__ void add_xor4(float4& acc, const float4& v, int m) {
-  acc.x += __shfl_xor_sync(0xffffffffu, v.x, m);
-  acc.y += __shfl_xor_sync(0xffffffffu, v.y, m);
-  acc.z += __shfl_xor_sync(0xffffffffu, v.z, m);
-  acc.w += __shfl_xor_sync(0xffffffffu, v.w, m);
-}
-
 // Sums one group's [channel][state] tile over the channels and adds state
 // row n's four steps into acc_b[n * L + t] (t = the group's first step).
 // Lane o + NS*h sums channels h*kS .. h*kS + kS - 1 of state o, then the
@@ -239,7 +250,7 @@ __global__ void __launch_bounds__(32)
   // channel bits 1 and 2, so that the first two shuffle levels exchange the
   // same slots on every lane.
   constexpr bool kShflFlush = NS == 16;
-  const int perm = kShflFlush ? (c >> 1) & 3 : 0;
+  const int perm = state_perm<NS>(c);
   auto st_of = [&](int j) { return q + kLPC * (j ^ perm); };
 
   int len = L;
@@ -331,8 +342,8 @@ __global__ void __launch_bounds__(32)
     float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
     float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
 
-    // ---- 2. the saved state entering each group, in the forward's slot
-    // order (lane q: state q + kLPC j' at slot j'); groups starting at or
+    // ---- 2. the saved state entering each group, in slot order (lane q,
+    // slot j: state st_of(j), as the forward keeps it); groups starting at or
     // past the valid length carry delta = 0 and only need a finite state.
     // The walk below prefetches two groups ahead so that the loads' latency
     // hides behind the work of the groups in between.
@@ -350,12 +361,12 @@ __global__ void __launch_bounds__(32)
             if constexpr (kS > 1) v.y = cs[1];
           }
         } else if (p.h0) {
-          const float* h0 = p.h0 + row * NS + q;
-          v.x = __ldg(h0);
-          if constexpr (kS > 1) v.y = __ldg(h0 + kLPC);
+          const float* h0 = p.h0 + row * NS;
+          v.x = __ldg(h0 + st_of(0));
+          if constexpr (kS > 1) v.y = __ldg(h0 + st_of(1));
           if constexpr (kS > 2) {
-            v.z = __ldg(h0 + 2 * kLPC);
-            v.w = __ldg(h0 + 3 * kLPC);
+            v.z = __ldg(h0 + st_of(2));
+            v.w = __ldg(h0 + st_of(3));
           }
         }
       }
@@ -446,11 +457,28 @@ __global__ void __launch_bounds__(32)
       }
     }
 
-    // u and delta_eff u (ZOH: u) of four steps; delta_eff is zero past the
-    // end, so delta_eff u is too (ZOH: b_bar = expm1(0) / A = 0)
-    auto load_dl_du = [&](int tg, float2 (&dlp)[2], float2 (&dup_)[2]) {
-      const float4 dl4 = ld4s(wD, c, tg);
-      const float4 u4 = ld4s(bU, c, tg);
+    // this lane's rows: channel c of the work rows and of u, states st_of(j)
+    // of B and C
+    float* const rD = wD + c * kBT;
+    float* const rY = wY + c * kBT;
+    T* const rU = bU + c * kBT;
+    T* const rDo = bD + c * kBT;  // ddelta out (in place of delta)
+    const int kW = row_key(wD, c), kU = row_key(bU, c);
+    const T* rB[kS];
+    int kB[kS];
+#pragma unroll
+    for (int j = 0; j < kS; ++j) {
+      rB[j] = bB + st_of(j) * kBT;
+      kB[j] = row_key(bB, st_of(j));
+    }
+    constexpr int kCfromB = Sh::kNSP * 2 * kBT;  // rawC[s] - rawB[s], elements
+    static_assert(offsetof(Sh, rawC) - offsetof(Sh, rawB) == kCfromB * sizeof(T), "B/C");
+
+    // delta_eff and delta_eff u (ZOH: u) of group g; delta_eff is zero past
+    // the end, so delta_eff u is too (ZOH: b_bar = expm1(0) / A = 0)
+    auto load_dl_du = [&](int g, float2 (&dlp)[2], float2 (&dup_)[2]) {
+      const float4 dl4 = ld4p(rD + grp_off(rD, kW, g));
+      const float4 u4 = ld4p(rU + grp_off(rU, kU, g));
       dlp[0] = make_float2(dl4.x, dl4.y);
       dlp[1] = make_float2(dl4.z, dl4.w);
       dup_[0] = make_float2(u4.x, u4.y);
@@ -469,8 +497,8 @@ __global__ void __launch_bounds__(32)
       carry1 = carry2;
       if (g >= 2) carry2 = load_carry(g - 2);
       float2 dlp[2], dup_[2];
-      load_dl_du(tg, dlp, dup_);
-      const float4 dy4 = ld4s(wY, c, tg);
+      load_dl_du(g, dlp, dup_);
+      const float4 dy4 = ld4p(rY + grp_off(rY, kW, g));
       const float2 dyp[2] = {make_float2(dy4.x, dy4.y), make_float2(dy4.z, dy4.w)};
       float2 gA[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g a h_{t-1} A
       float2 gB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g B (ZOH: g b_bar)
@@ -478,21 +506,15 @@ __global__ void __launch_bounds__(32)
 #pragma unroll
       for (int j = 0; j < kS; ++j) {
         const int n = st_of(j);
-        const float4 B4 = ld4s(bB, n, tg);
-        const float4 C4 = ld4s(bC, n, tg);
+        const int ob = grp_off(rB[j], kB[j], g);
+        const float4 B4 = ld4p(rB[j] + ob);
+        const float4 C4 = ld4p(rB[j] + kCfromB + ob);
         const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
         const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
         const float2 a2p = dup2(a2[j]);
-        // recompute a_t and h_t over the group (this lane's slot j is the
-        // forward's slot j ^ perm)
+        // recompute a_t and h_t over the group
         float2 ab[2], hv[2], bu[2], bb[2];
-        float hh;
-        {
-          const int sl = j ^ perm;
-          const float lo = (sl & 1) ? hcur.y : hcur.x;
-          const float hi = (sl & 1) ? hcur.w : hcur.z;
-          hh = (sl & 2) ? hi : lo;
-        }
+        float hh = j == 0 ? hcur.x : j == 1 ? hcur.y : j == 2 ? hcur.z : hcur.w;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float2 arg = mul2(dlp[e], a2p);
@@ -558,19 +580,20 @@ __global__ void __launch_bounds__(32)
       // the steps it emits), then du and ddelta for those steps
       const float fa[4] = {gA[0].x, gA[0].y, gA[1].x, gA[1].y};
       const float fb[4] = {gB[0].x, gB[0].y, gB[1].x, gB[1].y};
+      const int owd = grp_off(rD, kW, g), owu = grp_off(rU, kU, g);
       auto emit = [&](int e, float sa, float sb) {
         const int tl = tg + e;
         const bool valid = act && t0 + tl < len;
-        const float dlv = ld1s(wD, c, tl);
-        const float dyv = ld1s(wY, c, tl);
-        const float uv = ld1s(bU, c, tl);
+        const float dlv = rD[owd + e];
+        const float dyv = rY[owd + e];
+        const float uv = to_f32(rU[owu + e]);
         float gd = kZOH ? sa : fmaf(uv, sb, sa);
         if (p.delta_softplus) gd *= sigmoid_from_softplus(dlv);
         const float du = fmaf(Dv, dyv, kZOH ? sb : dlv * sb);
         gd = valid ? gd : 0.f;
         dbias_acc += gd;
-        st1s(bU, c, tl, valid ? du : 0.f);
-        st1s(bD, c, tl, gd);
+        rU[owu + e] = static_cast<T>(valid ? du : 0.f);
+        rDo[owu + e] = static_cast<T>(gd);
       };
       if constexpr (kLPC == 4) {
         const bool hi2 = (q & 2) != 0;

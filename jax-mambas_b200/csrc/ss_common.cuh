@@ -18,11 +18,20 @@ namespace mss {
 
 constexpr int kCkpt = MSS_CHUNK;  // steps per saved carry (chunk_states entry)
 
+// N = 16: the lane that owns states q, q + 4, q + 8, q + 12 of channel slot c
+// (of 8 in a CTA) keeps state q + 4 (j ^ state_perm(c)) in its slot j. Both
+// kernels use this order (the backward needs it for its shuffle sums of dB and
+// dC over channels), so saved carries need no reordering between them.
+template <int NS>
+__device__ __forceinline__ int state_perm(int c) {
+  return NS == 16 ? (c >> 1) & 3 : 0;
+}
+
 // Saved carries are (batch, n_chunks, dim, dstate) fp32, time-major so that a
 // warp's stores and loads of one carry index are contiguous. Inside a
-// (batch, index, channel) entry the states are in lane order: the lane that
-// owns states q, q + lpc, q + 2 lpc, ... (lpc lanes per channel) keeps them
-// at q * (dstate / lpc) + 0, 1, 2, ..., one 16-byte word for 4 states.
+// (batch, index, channel) entry the states are in lane-slot order: lane q's
+// slots 0, 1, 2, ... (states q + lpc (j ^ perm), lpc lanes per channel) sit at
+// q * (dstate / lpc) + 0, 1, 2, ..., one 16-byte word for 4 states.
 __device__ __forceinline__ size_t carry_offset(int b, int idx, int n_chunks, int dim, int d,
                                                int dstate) {
   return ((static_cast<size_t>(b) * n_chunks + idx) * dim + d) * dstate;
@@ -254,6 +263,16 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return __ffma2_rn(a, b, c);
 }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// acc += the partner lane's (lane ^ m) v, component-wise, with packed adds.
+__device__ __forceinline__ void add_xor4(float4& acc, const float4& v, int m) {
+  const float2 lo = add2(make_float2(acc.x, acc.y),
+                         make_float2(__shfl_xor_sync(0xffffffffu, v.x, m),
+                                     __shfl_xor_sync(0xffffffffu, v.y, m)));
+  const float2 hi = add2(make_float2(acc.z, acc.w),
+                         make_float2(__shfl_xor_sync(0xffffffffu, v.z, m),
+                                     __shfl_xor_sync(0xffffffffu, v.w, m)));
+  acc = make_float4(lo.x, lo.y, hi.x, hi.y);
+}
 __device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
 
 }  // namespace mss

@@ -28,6 +28,7 @@
 // staging done by plain loads instead of TMA.
 #include <cudaTypedefs.h>
 
+#include <cstddef>
 #include <cstring>
 
 #include "ss_common.cuh"
@@ -124,9 +125,12 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
   const int L = p.seqlen;
   const int n_ch = min(kCh, p.dim - d0);  // live channels of this CTA
 
-  // this lane's channel slot and states (lane q owns states q, q+kLPC, ...)
+  // this lane's channel slot and states: slot j holds state
+  // q + kLPC (j ^ perm) (a permutation of q, q + kLPC, ...; see state_perm)
   const int cl = warp * Cfg::kCPW + lane / kLPC;
   const int q = lane % kLPC;
+  const int perm = state_perm<NS>(cl);
+  auto st_of = [&](int j) { return q + kLPC * (j ^ perm); };
   const bool lane_active = cl < n_ch;
   const int d = d0 + (lane_active ? cl : 0);
   const size_t row = static_cast<size_t>(b) * p.dim + d;
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
   float a2[kS], Av[kS], h[kS];
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
-    const int n = q + kLPC * j;
+    const int n = st_of(j);
     Av[j] = __ldg(p.A + d * NS + n);
     a2[j] = Av[j] * kLog2e;
     h[j] = (lane_active && p.h0) ? __ldg(p.h0 + row * NS + n) : 0.f;
@@ -276,24 +280,38 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       // kLPC lanes of a channel read adjacent B/C rows (distinct banks) and
       // pairs of steps are packed into fp32x2 operations.
       const int steps = min(kTile, len - t0);
+      // this lane's rows (pointers and swizzle keys, fixed over the tile)
+      const float* rB[kS];
+      int kB[kS];
+#pragma unroll
+      for (int j = 0; j < kS; ++j) {
+        rB[j] = reinterpret_cast<const float*>(&sh.rawB[s][st_of(j)][0]);
+        kB[j] = st_of(j) & 7;
+      }
+      using Sh = FwdShared<NS, T>;
+      constexpr int kCfromB = 2 * Sh::kNSP * kTile;  // rawC - rawB, elements
+      static_assert(offsetof(Sh, rawC) - offsetof(Sh, rawB) == kCfromB * sizeof(T),
+                    "rawC follows rawB");
+      const float* const rdl = &sh.dlt[cl][0];
+      const float* const rdu = &sh.dlu[cl][0];
+      float* cs = p.chunk_states + carry_offset(b, t0 / kCkpt, p.n_chunks, p.dim, d, NS) + q * kS;
+      const size_t cs_step = static_cast<size_t>(p.dim) * NS;  // next carry index
 #pragma unroll 2
       for (int tt = 0; tt < steps; tt += 4) {
-        const float4 dl4 = *reinterpret_cast<const float4*>(&sh.dlt[cl][tt]);
-        const float4 du4 = *reinterpret_cast<const float4*>(&sh.dlu[cl][tt]);
+        const float4 dl4 = *reinterpret_cast<const float4*>(rdl + tt);
+        const float4 du4 = *reinterpret_cast<const float4*>(rdu + tt);
         const float2 dlp[2] = {make_float2(dl4.x, dl4.y), make_float2(dl4.z, dl4.w)};
         const float2 dup_[2] = {make_float2(du4.x, du4.y), make_float2(du4.z, du4.w)};
         float2 yp2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
-          const int n = q + kLPC * j;
+          const int n = st_of(j);
           float4 B4, C4;
           if constexpr (kDirectBC) {
             // 16-byte chunk tt/4 of row n sits at chunk (tt/4) ^ (n & 7)
-            const int col = ((tt >> 2) ^ (n & 7)) << 2;
-            B4 = *reinterpret_cast<const float4*>(
-                reinterpret_cast<const float*>(&sh.rawB[s][n][0]) + col);
-            C4 = *reinterpret_cast<const float4*>(
-                reinterpret_cast<const float*>(&sh.rawC[s][n][0]) + col);
+            const int col = ((tt >> 2) ^ kB[j]) << 2;
+            B4 = *reinterpret_cast<const float4*>(rB[j] + col);
+            C4 = *reinterpret_cast<const float4*>(rB[j] + kCfromB + col);
           } else {
             B4 = *reinterpret_cast<const float4*>(&sh.Bs[n][tt]);
             C4 = *reinterpret_cast<const float4*>(&sh.Cs[n][tt]);
@@ -349,8 +367,6 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
         // carry after these 4 steps (entries past the valid length are not
         // written: the backward never reads them)
         if (lane_active) {
-          float* cs = p.chunk_states + carry_offset(b, (t0 + tt) / kCkpt, p.n_chunks, p.dim, d, NS) +
-                      q * kS;
           if constexpr (kS == 4) {
             *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
           } else {
@@ -358,6 +374,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
             for (int j = 0; j < kS; ++j) cs[j] = h[j];
           }
         }
+        cs += cs_step;
       }
     }
 
@@ -406,7 +423,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
 
   if (p.last_state && lane_active) {
 #pragma unroll
-    for (int j = 0; j < kS; ++j) p.last_state[row * NS + q + kLPC * j] = h[j];
+    for (int j = 0; j < kS; ++j) p.last_state[row * NS + st_of(j)] = h[j];
   }
 }
 
