@@ -347,13 +347,16 @@ __global__ void __launch_bounds__(32)
     // past the valid length carry delta = 0 and only need a finite state.
     // The walk below prefetches two groups ahead so that the loads' latency
     // hides behind the work of the groups in between.
-    auto load_carry = [&](int g) {
+    // carry entering group g sits at carry index t0 / kCkpt + g - 1; the
+    // pointer below is that of group kNG - 1 and steps back one index per group
+    const size_t cs_step = static_cast<size_t>(p.dim) * NS;
+    const float* cs_g = p.chunk_states + q * kS +
+                        carry_offset(b, max(t0 / kCkpt + kNG - 2, 0), p.n_chunks, p.dim, d, NS);
+    auto load_carry = [&](int g, const float* cs) {
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       const int gi = t0 / kCkpt + g;  // carry index of the group
       if (act && t0 + g * kGrp < len) {
         if (gi > 0) {
-          const float* cs =
-              p.chunk_states + carry_offset(b, gi - 1, p.n_chunks, p.dim, d, NS) + q * kS;
           if constexpr (kS == 4) {
             v = *reinterpret_cast<const float4*>(cs);
           } else {
@@ -372,7 +375,12 @@ __global__ void __launch_bounds__(32)
       }
       return v;
     };
-    float4 carry1 = load_carry(kNG - 1), carry2 = load_carry(kNG - 2);
+    float4 carry1 = load_carry(kNG - 1, cs_g);
+    cs_g -= cs_step;
+    float4 carry2 = load_carry(kNG - 2, cs_g);
+    // dB/dC accumulator row of this lane's flush (N = 16: dB for channel bit
+    // 0 clear, dC for set; state st_of(0)), at the tile's first step
+    float* const acc_row = (((c & 1) != 0 ? dC_b : dB_b) + static_cast<size_t>(st_of(0)) * L) + t0;
 
     if (use_tma) {
       bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
@@ -495,13 +503,15 @@ __global__ void __launch_bounds__(32)
       const int tg = g * kGrp;
       const float4 hcur = carry1;
       carry1 = carry2;
-      if (g >= 2) carry2 = load_carry(g - 2);
+      if (g >= 2) {
+        cs_g -= cs_step;
+        carry2 = load_carry(g - 2, cs_g);
+      }
       float2 dlp[2], dup_[2];
       load_dl_du(g, dlp, dup_);
       const float4 dy4 = ld4p(rY + grp_off(rY, kW, g));
       const float2 dyp[2] = {make_float2(dy4.x, dy4.y), make_float2(dy4.z, dy4.w)};
-      float2 gA[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g a h_{t-1} A
-      float2 gB[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum_n g B (ZOH: g b_bar)
+      float2 gA[2], gB[2];  // sum_n g a h_{t-1} A, sum_n g B (ZOH: g b_bar); set by slot 0
       float4 dBq[kS], dCq[kS];
 #pragma unroll
       for (int j = 0; j < kS; ++j) {
@@ -545,7 +555,7 @@ __global__ void __launch_bounds__(32)
           // a_t h_{t-1} = h_t - b_t
           const float2 ah = add2(hv[e], make_float2(-bu[e].x, -bu[e].y));
           const float2 w = mul2(gv[e], ah);
-          gA[e] = fma2(w, dup2(Av[j]), gA[e]);
+          gA[e] = j == 0 ? mul2(w, dup2(Av[j])) : fma2(w, dup2(Av[j]), gA[e]);
           dAacc[j] = fma2(w, dlp[e], dAacc[j]);
           if constexpr (kZOH) {
             // d b_t/d delta = a_t B u, d b_t/d A = B u (delta a_t - b_bar) / A
@@ -554,10 +564,11 @@ __global__ void __launch_bounds__(32)
             const float inv = 1.f / Av[j];
             dAacc[j].x += gBu.x * (dlp[e].x * ab[e].x - bb[e].x) * inv;
             dAacc[j].y += gBu.y * (dlp[e].y * ab[e].y - bb[e].y) * inv;
-            gB[e] = fma2(gv[e], mul2(Bp[e], bb[e]), gB[e]);
+            gB[e] = j == 0 ? mul2(gv[e], mul2(Bp[e], bb[e]))
+                           : fma2(gv[e], mul2(Bp[e], bb[e]), gB[e]);
             dBv[e] = mul2(gv[e], mul2(bb[e], dup_[e]));
           } else {
-            gB[e] = fma2(gv[e], Bp[e], gB[e]);
+            gB[e] = j == 0 ? mul2(gv[e], Bp[e]) : fma2(gv[e], Bp[e], gB[e]);
             dBv[e] = mul2(gv[e], dup_[e]);
           }
           dCv[e] = mul2(dyp[e], hv[e]);
@@ -635,7 +646,7 @@ __global__ void __launch_bounds__(32)
         float4 keep = b0 ? dCq[0] : dBq[0];
         add_xor4(keep, b0 ? dBq[0] : dCq[0], 4);
         if (live) {
-          float* gp = (b0 ? dC_b : dB_b) + static_cast<size_t>(st_of(0)) * L + t0 + tg;
+          float* gp = acc_row + tg;
           if (whole) {
             atomicAdd(reinterpret_cast<float4*>(gp), keep);
           } else {
