@@ -121,17 +121,20 @@ def _algorithmic(cfg, esize, d=None):
     elems = b * d * L
     bnl = b * n * L
     nch = math.ceil(L / 4)  # saved carries per row (one per 4 steps)
-    cs = b * d * nch * n * 4
-    # forward: u, delta, z in; out and the pre-gate out (kept for dz) out
-    fwd = elems * 5 * esize + 2 * bnl * esize + cs
-    # backward: u, delta, z, dy, pre-gate out in; du, ddelta, dz out
-    bwd = elems * 8 * esize + 4 * bnl * esize + cs
+    # Algorithmic bytes (the minimum I/O of the fused op): forward u, delta,
+    # z, B, C in, out and the pre-gate out (kept for dz) out; backward u,
+    # delta, z, dy, pre-gate, B, C in, du, ddelta, dz, dB, dC out. The saved
+    # carries (fp32 state every 4 steps, written by the forward and read by
+    # the backward) are this design's own extra traffic, reported apart.
+    fwd = elems * 5 * esize + 2 * bnl * esize
+    bwd = elems * 8 * esize + 4 * bnl * esize
+    carry = b * d * nch * n * 4
     # special-function-unit ops per element: N ex2 per pass, plus softplus
-    # (exp, log), sigmoid(z) (exp, rcp) in the forward and softplus, sigmoid
-    # of delta and sigmoid(z) in the backward
+    # (exp, reciprocal) and sigmoid(z) (exp, reciprocal) in both kernels and
+    # the softplus derivative (exp) in the backward
     mufu_fwd = n + 4
-    mufu_bwd = n + 6
-    return elems, fwd, bwd, mufu_fwd, mufu_bwd
+    mufu_bwd = n + 5
+    return elems, fwd, bwd, carry, mufu_fwd, mufu_bwd
 
 
 def run_gpu(args, cfg):
@@ -241,13 +244,13 @@ def run_gpu(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
 
-    elems, fwd_bytes, bwd_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize, d)
+    elems, fwd_bytes, bwd_bytes, carry_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize, d)
     # padded steps are skipped by the kernels: the rooflines count
     # the valid steps only, the headline value counts every B*D*L position
     valid = 1.0
     if seq_lens is not None:
         valid = float(seq_lens.sum().item()) / (b * L)
-    fwd_bytes, bwd_bytes = fwd_bytes * valid, bwd_bytes * valid
+    fwd_bytes, bwd_bytes, carry_bytes = fwd_bytes * valid, bwd_bytes * valid, carry_bytes * valid
     ms_per_step = total_ms / args.steps
     total_elems = b * d_total * L if chan else elems * world
     value = total_elems / (ms_per_step * 1e-3) / 1e9
@@ -271,7 +274,7 @@ def run_gpu(args, cfg):
     if traffic is None and args.config == "c1":
         tf = ROOT / "profiles" / "ncu_traffic.json"
         if tf.exists():
-            traffic = json.loads(tf.read_text()).get("c1", {}).get("ss_bwd_kernel")
+            traffic = json.loads(tf.read_text()).get("c1", {}).get("ss_bwd_tile_kernel")
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -285,12 +288,13 @@ def run_gpu(args, cfg):
                          f"{elems * esize * 4 / 1e6:.0f} MB per step)",
                    "valid_fraction": round(valid, 4)},
         "kernels_ms": {"fwd": round(fwd_ms, 4), "bwd": round(bwd_ms, 4)},
-        "roofline": {"bound": "hbm", "kernel": "ss_bwd_kernel",
+        "roofline": {"bound": "hbm", "kernel": "ss_bwd_tile_kernel",
                      "achieved": round(bwd_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(bwd_gbs / hbm, 4), "traffic": traffic,
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_src == "measured" else "fallback 6.65 TB/s",
-                     "algorithmic_bytes_per_launch": bwd_bytes},
+                     "algorithmic_bytes_per_launch": bwd_bytes,
+                     "carry_bytes_per_launch": carry_bytes},
         "roofline_fwd": {"bound": "hbm", "kernel": "ss_fwd_kernel", "achieved": round(fwd_gbs, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(fwd_gbs / hbm, 4)},
         "roofline_sfu": {"bound": "sfu", "unit": "MUFU op/s",
