@@ -170,18 +170,20 @@ __device__ void unstage_tile_plain(T* base, const T* tile, size_t row0, int n_va
   }
 }
 
-// Zeroes steps [from, L) of n rows (one warp); 16-byte stores when `vec`.
+// Zeroes steps [from, to) of n rows of length L (one warp); 16-byte stores
+// when `vec` (from and to multiples of 16 bytes).
 template <typename T>
-__device__ void zero_rows(T* base, size_t row0, int n, int L, int from, bool vec, int lane) {
-  if (from >= L) return;
+__device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, bool vec,
+                          int lane) {
+  if (from >= to) return;
   constexpr int kPer = 16 / sizeof(T);
   for (int r = 0; r < n; ++r) {
     T* rowp = base + (row0 + r) * static_cast<size_t>(L);
     if (vec) {
-      for (int t = from + lane * kPer; t < L; t += 32 * kPer)
+      for (int t = from + lane * kPer; t < to; t += 32 * kPer)
         *reinterpret_cast<uint4*>(rowp + t) = make_uint4(0u, 0u, 0u, 0u);
     } else {
-      for (int t = from + lane; t < L; t += 32) rowp[t] = static_cast<T>(0.f);
+      for (int t = from + lane; t < to; t += 32) rowp[t] = static_cast<T>(0.f);
     }
   }
 }
@@ -223,7 +225,9 @@ __device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_
   }
 }
 
-template <int NS, typename T, bool kZOH>
+// kSeg: the launch is cut into time segments (blockIdx.z); without it the
+// segment bounds are compile-time constants (one segment of the whole row).
+template <int NS, typename T, bool kZOH, bool kSeg>
 __global__ void __launch_bounds__(32)
     ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
   using Cfg = TileCfg<NS>;
@@ -255,7 +259,14 @@ __global__ void __launch_bounds__(32)
 
   int len = L;
   if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
-  const int k_last = len > 0 ? (len - 1) / kBT : -1;  // last tile with valid steps
+  // this CTA's time segment: tiles [k_begin, k_end); k_last is the last tile
+  // of it with valid steps (k_last < k_begin: none)
+  const int seg = kSeg ? static_cast<int>(blockIdx.z) : 0;
+  const int n_seg = kSeg ? p.n_seg : 1;
+  const int k_begin = kSeg ? seg * p.seg_tiles : 0;
+  const int k_end = kSeg ? min((L + kBT - 1) / kBT, k_begin + p.seg_tiles) : (L + kBT - 1) / kBT;
+  const int k_last = len > 0 ? min((len - 1) / kBT, k_end - 1) : k_begin - 1;
+  const size_t seg_row = row * n_seg + seg;
   const bool use_tma = p.tma_ok != 0;
   const bool tma_store = use_tma && n_ch == kCh;  // whole boxes stay in this batch
   const bool has_z = p.z != nullptr;
@@ -271,11 +282,12 @@ __global__ void __launch_bounds__(32)
 
   // Steps past the last valid tile are padding: their gradients are zero.
   {
-    const int tz = (k_last + 1) * kBT;
+    const int tz = max(k_last + 1, k_begin) * kBT;
+    const int te = min(k_end * kBT, L);
     const bool vec = use_tma;  // 16-byte aligned rows (L * esize % 16 == 0)
-    zero_rows(static_cast<T*>(p.du), row0, n_ch, L, tz, vec, lane);
-    zero_rows(static_cast<T*>(p.ddelta), row0, n_ch, L, tz, vec, lane);
-    if (has_z) zero_rows(static_cast<T*>(p.dz), row0, n_ch, L, tz, vec, lane);
+    zero_rows(static_cast<T*>(p.du), row0, n_ch, L, tz, te, vec, lane);
+    zero_rows(static_cast<T*>(p.ddelta), row0, n_ch, L, tz, te, vec, lane);
+    if (has_z) zero_rows(static_cast<T*>(p.dz), row0, n_ch, L, tz, te, vec, lane);
   }
 
   // TMA pipeline: position i of the walk is tile k_last - i; its arrays go
@@ -305,11 +317,11 @@ __global__ void __launch_bounds__(32)
     mbar_init(&sh.bar[1], 1);
     mbar_init(&sh.barP, 1);
     fence_mbar_init();
-    if (k_last >= 0) {
+    if (k_last >= k_begin) {
       issue(0);
       if (has_z) issue_pre(0);
     }
-    if (k_last >= 1) issue(1);
+    if (k_last >= k_begin + 1) issue(1);
   }
   __syncwarp();
 
@@ -318,7 +330,12 @@ __global__ void __launch_bounds__(32)
   float2 dAacc[kS];
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
-    gn[j] = (act && p.dlast) ? __ldg(p.dlast + row * NS + st_of(j)) : 0.f;
+    // the last segment starts from dlast, the others from the carry their
+    // right neighbours pass
+    if (kSeg && seg < n_seg - 1)
+      gn[j] = act ? p.seg_carry[seg_row * NS + st_of(j)] : 0.f;
+    else
+      gn[j] = (act && p.dlast) ? __ldg(p.dlast + row * NS + st_of(j)) : 0.f;
     an[j] = 1.f;
     dAacc[j] = make_float2(0.f, 0.f);
   }
@@ -328,7 +345,7 @@ __global__ void __launch_bounds__(32)
   float* dB_b = p.dB_acc + static_cast<size_t>(b) * NS * L;
   float* dC_b = p.dC_acc + static_cast<size_t>(b) * NS * L;
 
-  for (int k = k_last; k >= 0; --k) {
+  for (int k = k_last; k >= k_begin; --k) {
     const int i = k_last - k;
     const int s = i & 1;
     const int t0 = k * kBT;
@@ -391,7 +408,7 @@ __global__ void __launch_bounds__(32)
           // let the copies in flight land before the CTA exits
           mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
           if (has_z) mbar_wait_bounded(&sh.barP, i & 1);
-          if (i == 0 && k >= 1) mbar_wait_bounded(&sh.bar[1], 0);
+          if (i == 0 && k > k_begin) mbar_wait_bounded(&sh.bar[1], 0);
           bulk_wait_all();
         }
         return;
@@ -454,7 +471,7 @@ __global__ void __launch_bounds__(32)
     }
     __syncwarp();
 
-    if (use_tma && lane == 0 && k >= 1) {
+    if (use_tma && lane == 0 && k > k_begin) {
       fence_proxy_async_smem();  // the warp's reads of rawP are done
       if (has_z) issue_pre(i + 1);
       // the other buffer held the previous position's du/ddelta/dz for its
@@ -696,17 +713,219 @@ __global__ void __launch_bounds__(32)
     dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, m);
     dbias_acc += __shfl_xor_sync(0xffffffffu, dbias_acc, m);
   }
+  // partial sums of this (segment, batch, channel)
+  const size_t prow = static_cast<size_t>(seg) * p.batch * p.dim + row;
   if (act) {
 #pragma unroll
     for (int j = 0; j < kS; ++j) {
       const int n = st_of(j);
-      p.dA_part[row * NS + n] = dAacc[j].x + dAacc[j].y;
-      if (p.dh0) p.dh0[row * NS + n] = an[j] * gn[j];
+      p.dA_part[prow * NS + n] = dAacc[j].x + dAacc[j].y;
+      if (p.dh0 && seg == 0) p.dh0[row * NS + n] = an[j] * gn[j];
     }
     if (q == 0) {
-      p.dD_part[row] = dD_acc;
-      p.dbias_part[row] = dbias_acc;
+      p.dD_part[prow] = dD_acc;
+      p.dbias_part[prow] = dbias_acc;
     }
+  }
+}
+
+
+// Adjoint pass of a segmented backward. For segment s = blockIdx.z + 1 it
+// runs g_t = dy_t C_t + a_{t+1} g_{t+1} over the segment from g = 0 past its
+// end, and writes the carry a_t0 g_t0 that the segment passes to its left
+// neighbour in that case (seg_G) and its sum of delta_eff (seg_dsum); the
+// carry with a nonzero right seed X is seg_G + 2^(A log2 e dsum) X. Same
+// lanes, staging (delta, dout, z and C only) and transform as the main pass.
+template <int NS, typename T>
+__global__ void __launch_bounds__(32)
+    ss_bwd_segadj_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
+  using Cfg = TileCfg<NS>;
+  using Sh = TileShared<NS, T>;
+  constexpr int kS = Cfg::kS;
+  constexpr int kLPC = Cfg::kLPC;
+  constexpr int kCh = Cfg::kCh;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
+
+  const int lane = threadIdx.x;
+  const int b = blockIdx.y;
+  const int d0 = blockIdx.x * kCh;
+  const int L = p.seqlen;
+  const int n_ch = min(kCh, p.dim - d0);
+  const int c = lane / kLPC;
+  const int q = lane % kLPC;
+  const bool act = c < n_ch;
+  const int d = d0 + (act ? c : 0);
+  const size_t row = static_cast<size_t>(b) * p.dim + d;
+  const size_t row0 = static_cast<size_t>(b) * p.dim + d0;
+  const int perm = state_perm<NS>(c);
+  auto st_of = [&](int j) { return q + kLPC * (j ^ perm); };
+
+  int len = L;
+  if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
+  const int seg = blockIdx.z + 1;
+  const size_t seg_row = row * p.n_seg + seg;
+  const int k_begin = seg * p.seg_tiles;
+  const int k_end = min((L + kBT - 1) / kBT, k_begin + p.seg_tiles);
+  const int k_last = len > 0 ? min((len - 1) / kBT, k_end - 1) : k_begin - 1;
+  const bool use_tma = p.tma_ok != 0;
+  const bool has_z = p.z != nullptr;
+
+  float a2[kS];
+#pragma unroll
+  for (int j = 0; j < kS; ++j) a2[j] = __ldg(p.A + d * NS + st_of(j)) * kLog2e;
+  const float bias = p.delta_bias ? __ldg(p.delta_bias + d) : 0.f;
+
+  constexpr uint32_t kChBytes = kCh * kBT * sizeof(T);
+  constexpr uint32_t kNBytes = NS * kBT * sizeof(T);
+  const int rc = static_cast<int>(row0);
+  auto issue = [&](int i) {  // one thread: position i = tile k_last - i
+    const int s = i & 1;
+    const int x = (k_last - i) * kBT;
+    uint64_t* bar = &sh.bar[s];
+    mbar_arrive_expect_tx(bar, (has_z ? 3u : 2u) * kChBytes + kNBytes);
+    tma_load_2d(&sh.rawD[s][0][0], &maps.d, x, rc, bar);
+    tma_load_2d(&sh.rawY[s][0][0], &maps.y, x, rc, bar);
+    if (has_z) tma_load_2d(&sh.rawZ[s][0][0], &maps.z, x, rc, bar);
+    tma_load_2d(&sh.rawC[s][0][0], &maps.c, x, b * NS, bar);
+  };
+  if (use_tma && lane == 0) {
+    mbar_init(&sh.bar[0], 1);
+    mbar_init(&sh.bar[1], 1);
+    fence_mbar_init();
+    if (k_last >= k_begin) issue(0);
+  }
+  __syncwarp();
+
+  float G[kS];  // a_t g_t of the step just processed (0 past the segment end)
+#pragma unroll
+  for (int j = 0; j < kS; ++j) G[j] = 0.f;
+  float dsum = 0.f;
+
+  for (int k = k_last; k >= k_begin; --k) {
+    const int i = k_last - k;
+    const int s = i & 1;
+    const int t0 = k * kBT;
+    T* bD = &sh.rawD[s][0][0];
+    T* bY = &sh.rawY[s][0][0];
+    T* bZ = &sh.rawZ[s][0][0];
+    const T* bC = &sh.rawC[s][0][0];
+    float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
+    float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
+    if (use_tma) {
+      if (lane == 0 && k > k_begin) {
+        fence_proxy_async_smem();  // the warp is done with the other buffer
+        issue(i + 1);
+      }
+      const bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) {
+          atomicOr(&g_bwd_device_error, kErrTmaTimeout);
+          mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
+          if (k > k_begin) mbar_wait_bounded(&sh.bar[s ^ 1], ((i + 1) >> 1) & 1);
+        }
+        return;
+      }
+    } else {
+      stage_tile_plain(bD, static_cast<const T*>(p.delta), row0, n_ch, kCh, L, t0, lane);
+      stage_tile_plain(bY, static_cast<const T*>(p.dout), row0, n_ch, kCh, L, t0, lane);
+      if (has_z)
+        stage_tile_plain(bZ, static_cast<const T*>(p.z), row0, n_ch, kCh, L, t0, lane);
+      stage_tile_plain(&sh.rawC[s][0][0], static_cast<const T*>(p.C),
+                           static_cast<size_t>(b) * NS, NS, NS, L, t0, lane);
+      __syncwarp();
+    }
+
+    // transform: delta_eff and dy = dout silu(z), zero past the end
+    {
+      constexpr int kQ = kBT / 4 / kLPC;
+#pragma unroll
+      for (int qq = 0; qq < kQ; ++qq) {
+        const int tt = (q * kQ + qq) * 4;
+        const float4 x4 = ld4s(bD, c, tt);
+        const float4 y4 = ld4s(bY, c, tt);
+        float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_z) z4 = ld4s(bZ, c, tt);
+        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+        const float ys[4] = {y4.x, y4.y, y4.z, y4.w};
+        const float zs[4] = {z4.x, z4.y, z4.z, z4.w};
+        float dl[4], dy[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool valid = act && t0 + tt + e < len;
+          float xe = xs[e] + bias;
+          if (p.delta_softplus) xe = softplus_f(xe);
+          float ye = ys[e];
+          if (has_z) ye *= silu_f(zs[e]);
+          dl[e] = valid ? xe : 0.f;
+          dy[e] = valid ? ye : 0.f;
+        }
+        st4s(wD, c, tt, make_float4(dl[0], dl[1], dl[2], dl[3]));
+        st4s(wY, c, tt, make_float4(dy[0], dy[1], dy[2], dy[3]));
+      }
+    }
+    __syncwarp();
+
+    const float* rD = wD + c * kBT;
+    const float* rY = wY + c * kBT;
+    const int kW = row_key(wD, c);
+    const T* rC[kS];
+    int kC[kS];
+#pragma unroll
+    for (int j = 0; j < kS; ++j) {
+      rC[j] = bC + st_of(j) * kBT;
+      kC[j] = row_key(bC, st_of(j));
+    }
+#pragma unroll 2
+    for (int g = kNG - 1; g >= 0; --g) {
+      const int ow = grp_off(rD, kW, g);
+      const float4 dl4 = ld4p(rD + ow);
+      const float4 dy4 = ld4p(rY + ow);
+      dsum += (dl4.x + dl4.y) + (dl4.z + dl4.w);
+      const float2 dlp[2] = {make_float2(dl4.x, dl4.y), make_float2(dl4.z, dl4.w)};
+      const float2 dyp[2] = {make_float2(dy4.x, dy4.y), make_float2(dy4.z, dy4.w)};
+#pragma unroll
+      for (int j = 0; j < kS; ++j) {
+        const float4 C4 = ld4p(rC[j] + grp_off(rC[j], kC[j], g));
+        const float2 e0 = mul2(dyp[0], make_float2(C4.x, C4.y));
+        const float2 e1 = mul2(dyp[1], make_float2(C4.z, C4.w));
+        const float2 a0 = mul2(dlp[0], dup2(a2[j])), a1 = mul2(dlp[1], dup2(a2[j]));
+        // latest step first: g_t = e_t + G, then G = a_t g_t
+        float gg = G[j];
+        gg = ex2(a1.y) * (e1.y + gg);
+        gg = ex2(a1.x) * (e1.x + gg);
+        gg = ex2(a0.y) * (e0.y + gg);
+        gg = ex2(a0.x) * (e0.x + gg);
+        G[j] = gg;
+      }
+    }
+    __syncwarp();  // the other buffer is refilled next
+  }
+  if (act) {
+#pragma unroll
+    for (int j = 0; j < kS; ++j) p.seg_G[seg_row * NS + st_of(j)] = G[j];
+    if (q == 0) p.seg_dsum[seg_row] = dsum;
+  }
+}
+
+// Seeds of the backward's segments, right to left: segment n_seg - 1 starts
+// from dlast, segment s - 1 from seg_G(s) + 2^(A log2 e dsum(s)) seed(s).
+// One thread per (batch, channel, state).
+__global__ void seg_combine_bwd_kernel(const float* __restrict__ A, const float* __restrict__ dlast,
+                                       const float* __restrict__ seg_G,
+                                       const float* __restrict__ seg_dsum, float* seg_carry,
+                                       int batch, int dim, int dstate, int n_seg) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<long long>(batch) * dim * dstate) return;
+  const int n = static_cast<int>(i % dstate);
+  const long long bd = i / dstate;
+  const int d = static_cast<int>(bd % dim);
+  const float a2 = A[static_cast<size_t>(d) * dstate + n] * kLog2e;
+  float x = dlast ? dlast[i] : 0.f;
+  for (int s = n_seg - 1; s >= 0; --s) {
+    const size_t sr = static_cast<size_t>(bd) * n_seg + s;
+    seg_carry[sr * dstate + n] = x;
+    if (s > 0) x = fmaf(exp2f(a2 * seg_dsum[sr]), x, seg_G[sr * dstate + n]);
   }
 }
 
@@ -760,12 +979,31 @@ static cudaError_t launch_bwd_tile_t(const BwdParams& p, const TileMaps& maps,
   // the bytes in use: sizeof() would round up to the 1024-byte alignment
   using Sh = TileShared<NS, T>;
   const size_t smem = offsetof(Sh, barP) + sizeof(uint64_t);
-  auto kern = ss_bwd_tile_kernel<NS, T, kZOH>;
+  auto kern = ss_bwd_tile_kernel<NS, T, kZOH, false>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  dim3 grid((p.dim + TileCfg<NS>::kCh - 1) / TileCfg<NS>::kCh, p.batch);
-  kern<<<grid, 32, smem, stream>>>(p, maps);
+  const unsigned gx = (p.dim + TileCfg<NS>::kCh - 1) / TileCfg<NS>::kCh;
+  if (p.n_seg > 1) {
+    // the segments' seeds: adjoint pass (segments 1 ..), then the combine
+    auto kern_adj = ss_bwd_segadj_kernel<NS, T>;
+    e = cudaFuncSetAttribute(kern_adj, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kern_adj<<<dim3(gx, p.batch, p.n_seg - 1), 32, smem, stream>>>(p, maps);
+    const long long total = static_cast<long long>(p.batch) * p.dim * NS;
+    seg_combine_bwd_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        p.A, p.dlast, p.seg_G, p.seg_dsum, p.seg_carry, p.batch, p.dim, NS, p.n_seg);
+  }
+  if (p.n_seg > 1) {
+    auto kern_seg = ss_bwd_tile_kernel<NS, T, kZOH, true>;
+    e = cudaFuncSetAttribute(kern_seg, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kern_seg<<<dim3(gx, p.batch, p.n_seg), 32, smem, stream>>>(p, maps);
+  } else {
+    kern<<<dim3(gx, p.batch, 1), 32, smem, stream>>>(p, maps);
+  }
   return cudaPeekAtLastError();
 }
 
@@ -791,6 +1029,9 @@ static int tile_channels(int dstate) {
     default: return TileCfg<16>::kCh;
   }
 }
+static_assert(TileCfg<16>::kCh == 8 && TileCfg<8>::kCh == 16 && TileCfg<4>::kCh == 32 &&
+                  TileCfg<2>::kCh == 32 && TileCfg<1>::kCh == 32 && kBT == kScanTile,
+              "seg_plan's CTA count");
 
 // A row-major (rows x L) operand in boxes of box_rows rows x kBT steps,
 // 128-byte swizzle for fp32 rows, 64-byte for bf16 (TileShared's layout).
@@ -868,8 +1109,9 @@ static cudaError_t launch_bwd_finish(const BwdParams& p, int dstate, int io_dtyp
     const int total = p.dim * dstate + 2 * p.dim;
     const int threads = 256;
     const int blocks = (total + threads - 1) / threads;
+    // partials are per (segment, batch): n_seg * batch rows
     reduce_params_kernel<<<blocks, threads, 0, stream>>>(
-        p.dA_part, p.dD_part, p.dbias_part, dA, dD, ddelta_bias, p.batch,
+        p.dA_part, p.dD_part, p.dbias_part, dA, dD, ddelta_bias, p.batch * p.n_seg,
         p.dim, dstate);
     e = cudaPeekAtLastError();
     if (e != cudaSuccess) return e;

@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <string>
 
 #include "ss_launch.h"
@@ -52,19 +53,34 @@ int n_chunks_of(int length) { return (length + mss::kCkpt - 1) / mss::kCkpt; }
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 struct BwdWorkspace {
-  size_t dA_part, dD_part, dbias_part, dB_acc, dC_acc, total;
+  int n_seg, seg_tiles;
+  size_t dA_part, dD_part, dbias_part, seg_G, seg_dsum, seg_carry, dB_acc, dC_acc, total;
 };
 
 BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
                         int io_dtype) {
   BwdWorkspace w{};
+  const mss::SegPlan sp = mss::seg_plan(batch, length, dim, dstate);
+  w.n_seg = sp.n_seg;
+  w.seg_tiles = sp.seg_tiles;
+  // per (segment, batch) partial sums of dA, dD, ddelta_bias
+  const size_t sbd = static_cast<size_t>(sp.n_seg) * batch * dim;
   size_t off = 0;
   w.dA_part = off;
-  off += align256(sizeof(float) * static_cast<size_t>(batch) * dim * dstate);
+  off += align256(sizeof(float) * sbd * dstate);
   w.dD_part = off;
-  off += align256(sizeof(float) * static_cast<size_t>(batch) * dim);
+  off += align256(sizeof(float) * sbd);
   w.dbias_part = off;
-  off += align256(sizeof(float) * static_cast<size_t>(batch) * dim);
+  off += align256(sizeof(float) * sbd);
+  w.seg_G = w.seg_dsum = w.seg_carry = 0;
+  if (sp.n_seg > 1) {
+    w.seg_G = off;
+    off += align256(sizeof(float) * sbd * dstate);
+    w.seg_dsum = off;
+    off += align256(sizeof(float) * sbd);
+    w.seg_carry = off;
+    off += align256(sizeof(float) * sbd * dstate);
+  }
   w.dB_acc = w.dC_acc = 0;
   if (io_dtype == MSS_BF16) {
     const size_t bnl =
@@ -82,6 +98,36 @@ BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
 
 namespace mss {
 mss_status set_error(mss_status code, const std::string& msg) { return fail(code, msg); }
+
+SegPlan seg_plan(int batch, int length, int dim, int dstate) {
+  const int n_tiles = (length + kScanTile - 1) / kScanTile;
+  const int ch = scan_channels_per_cta(dstate);
+  const long long ctas = static_cast<long long>(batch) * ((dim + ch - 1) / ch);
+  // about 11 CTAs per SM are resident; more segments than one wave's worth
+  // still pay (shorter, better balanced work units) until the adjoint and
+  // end-state passes (which re-read most of the inputs) dominate; segments
+  // of at least 8 tiles
+  constexpr long long kTarget = 148 * 18;
+  int n = 1;
+  if (const char* env = getenv("MAMBA_SS_SEGMENTS")) {
+    n = std::max(1, atoi(env));
+  } else if (ctas < kTarget / 2) {
+    n = static_cast<int>(std::min<long long>(kTarget / std::max(1LL, ctas), n_tiles / 8));
+  }
+  n = std::max(1, std::min(n, n_tiles));
+  SegPlan sp;
+  sp.seg_tiles = (n_tiles + n - 1) / n;
+  sp.n_seg = (n_tiles + sp.seg_tiles - 1) / sp.seg_tiles;
+  return sp;
+}
+
+size_t fwd_seg_scratch_elems(int batch, int length, int dim, int dstate) {
+  const SegPlan sp = seg_plan(batch, length, dim, dstate);
+  if (sp.n_seg <= 1) return 0;
+  // end states and entering states (batch, dim, n_seg, dstate), delta sums
+  const size_t bds = static_cast<size_t>(batch) * dim * sp.n_seg;
+  return bds * (2 * static_cast<size_t>(dstate) + 1);
+}
 }  // namespace mss
 
 extern "C" {
@@ -97,7 +143,8 @@ uint32_t mamba_ss_take_device_error(void) {
 int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
                                     int32_t dstate) {
   if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
-  return static_cast<int64_t>(batch) * dim * n_chunks_of(length) * dstate;
+  return static_cast<int64_t>(batch) * dim * n_chunks_of(length) * dstate +
+         static_cast<int64_t>(mss::fwd_seg_scratch_elems(batch, length, dim, dstate));
 }
 
 size_t mamba_ss_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
@@ -206,6 +253,13 @@ mss_status mamba_ss_fused_bwd(
   p.dA_part = reinterpret_cast<float*>(ws + w.dA_part);
   p.dD_part = reinterpret_cast<float*>(ws + w.dD_part);
   p.dbias_part = reinterpret_cast<float*>(ws + w.dbias_part);
+  p.n_seg = w.n_seg;
+  p.seg_tiles = w.seg_tiles;
+  if (w.n_seg > 1) {
+    p.seg_G = reinterpret_cast<float*>(ws + w.seg_G);
+    p.seg_dsum = reinterpret_cast<float*>(ws + w.seg_dsum);
+    p.seg_carry = reinterpret_cast<float*>(ws + w.seg_carry);
+  }
   if (io_dtype == MSS_BF16) {
     p.dB_acc = reinterpret_cast<float*>(ws + w.dB_acc);
     p.dC_acc = reinterpret_cast<float*>(ws + w.dC_acc);

@@ -56,6 +56,14 @@ struct FwdParams {
   void* out_pre;  // optional: y + D*u before the gate (read by the backward for dz)
   float* last_state;
   float* chunk_states;
+  // time segments (n_seg > 1: see seg_plan): blockIdx.z is the segment, of
+  // seg_tiles tiles. The end-state pass writes seg_end (batch, dim, n_seg,
+  // dstate) and seg_dsum (batch, dim, n_seg); the main pass starts segment
+  // s > 0 from seg_in (batch, dim, n_seg, dstate).
+  int n_seg, seg_tiles;
+  float* seg_end;
+  float* seg_dsum;
+  const float* seg_in;
 };
 
 struct BwdParams {
@@ -81,10 +89,19 @@ struct BwdParams {
   void* dz;
   float* dB_acc;   // fp32 (batch, dstate, L), zeroed before the launch
   float* dC_acc;
-  float* dA_part;  // fp32 (batch, dim, dstate): per-batch partial sums
-  float* dD_part;  // fp32 (batch, dim)
+  float* dA_part;  // fp32 (n_seg, batch, dim, dstate): per-batch partial sums
+  float* dD_part;  // fp32 (n_seg, batch, dim)
   float* dbias_part;
   float* dh0;
+  // time segments (n_seg > 1: see seg_plan): blockIdx.z is the segment, of
+  // seg_tiles tiles. The adjoint pass writes seg_G (batch, dim, n_seg,
+  // dstate: the carry a_t0 g_t0 a segment passes left when nothing enters it
+  // from the right) and seg_dsum; the main pass seeds segment s < n_seg - 1
+  // with seg_carry (batch, dim, n_seg, dstate).
+  int n_seg, seg_tiles;
+  float* seg_G;
+  float* seg_dsum;
+  float* seg_carry;
 };
 
 struct StepParams {

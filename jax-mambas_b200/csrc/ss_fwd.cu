@@ -102,7 +102,9 @@ __device__ __forceinline__ void store4_global(__nv_bfloat16* dst, const float (&
   *reinterpret_cast<uint2*>(dst) = w;
 }
 
-template <int NS, typename T, bool kZOH>
+// kEnd: the end-state pass of a segmented scan (no outputs; each segment from
+// a zero state, its final state and sum of delta_eff to seg_end / seg_dsum).
+template <int NS, typename T, bool kZOH, bool kEnd>
 __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
     ss_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   using Cfg = FwdCfg<NS>;
@@ -138,14 +140,28 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
   int len = L;
   if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
 
+  // this CTA's time segment: tiles [k_begin, k_end)
+  const int seg = blockIdx.z;
+  const int k_begin = seg * p.seg_tiles;
+  const int k_end = min((L + kTile - 1) / kTile, k_begin + p.seg_tiles);
+  const size_t seg_row = row * p.n_seg + seg;
+
   float a2[kS], Av[kS], h[kS];
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
     const int n = st_of(j);
     Av[j] = __ldg(p.A + d * NS + n);
     a2[j] = Av[j] * kLog2e;
-    h[j] = (lane_active && p.h0) ? __ldg(p.h0 + row * NS + n) : 0.f;
+    float h0 = 0.f;
+    if (!kEnd && lane_active) {
+      if (seg > 0)
+        h0 = p.seg_in[seg_row * NS + n];
+      else if (p.h0)
+        h0 = __ldg(p.h0 + row * NS + n);
+    }
+    h[j] = h0;
   }
+  float dsum = 0.f;  // kEnd: sum of delta_eff over the segment
 
   const size_t bdl = static_cast<size_t>(b) * p.dim * L;
   const T* u_b = static_cast<const T*>(p.u) + bdl;
@@ -157,9 +173,10 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
   const T* C_b = static_cast<const T*>(p.C) + static_cast<size_t>(b) * NS * L;
   const bool use_tma = p.tma_ok != 0;
 
-  // Issues the TMA copies of tile `k` into staging buffer k % 2 (one thread).
+  // Issues the TMA copies of tile `k` into staging buffer (k - k_begin) % 2
+  // (one thread). The end-state pass needs neither z nor C.
   auto issue = [&](int k) {
-    const int s = k & 1;
+    const int s = (k - k_begin) & 1;
     const int t0 = k * kTile;
     uint64_t* bar = &sh.bar[s];
     if (t0 >= len) {
@@ -168,16 +185,16 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
     }
     constexpr uint32_t kChBytes = kCh * kTile * sizeof(T);
     constexpr uint32_t kNBytes = NS * kTile * sizeof(T);
-    mbar_arrive_expect_tx(bar, (z_b ? 3 : 2) * kChBytes + 2 * kNBytes);
+    const bool with_z = z_b && !kEnd;
+    mbar_arrive_expect_tx(bar, (with_z ? 3 : 2) * kChBytes + (kEnd ? 1 : 2) * kNBytes);
     const int rc = b * p.dim + d0;  // first channel row
     tma_load_2d(&sh.rawD[s][0][0], &maps.d, t0, rc, bar);
     tma_load_2d(&sh.rawU[s][0][0], &maps.u, t0, rc, bar);
-    if (z_b) tma_load_2d(&sh.rawZ[s][0][0], &maps.z, t0, rc, bar);
+    if (with_z) tma_load_2d(&sh.rawZ[s][0][0], &maps.z, t0, rc, bar);
     tma_load_2d(&sh.rawB[s][0][0], &maps.b, t0, b * NS, bar);
-    tma_load_2d(&sh.rawC[s][0][0], &maps.c, t0, b * NS, bar);
+    if (!kEnd) tma_load_2d(&sh.rawC[s][0][0], &maps.c, t0, b * NS, bar);
   };
 
-  const int n_tiles = (L + kTile - 1) / kTile;
   if (use_tma) {
     if (tid == 0) {
       mbar_init(&sh.bar[0], 1);
@@ -185,24 +202,25 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) issue(0);
+    if (tid == 0 && k_begin < k_end) issue(k_begin);
   }
 
-  for (int k = 0; k < n_tiles; ++k) {
-    const int s = k & 1;
+  for (int k = k_begin; k < k_end; ++k) {
+    const int kk = k - k_begin;  // position in the segment
+    const int s = kk & 1;
     const int t0 = k * kTile;
     if (use_tma) {
-      if (tid == 0 && k + 1 < n_tiles) {
+      if (tid == 0 && k + 1 < k_end) {
         fence_proxy_async_smem();  // the previous reads of that buffer are done
         issue(k + 1);
       }
-      const bool ok = mbar_wait_bounded(&sh.bar[s], (k >> 1) & 1);
+      const bool ok = mbar_wait_bounded(&sh.bar[s], (kk >> 1) & 1);
       if (__syncthreads_or(!ok)) {
         // A copy never completed: report it, let the in-flight copies of the
         // other buffer finish (bounded), and leave.
         if (tid == 0) {
           atomicOr(&g_fwd_device_error, kErrTmaTimeout);
-          if (k + 1 < n_tiles) mbar_wait_bounded(&sh.bar[s ^ 1], ((k + 1) >> 1) & 1);
+          if (k + 1 < k_end) mbar_wait_bounded(&sh.bar[s ^ 1], ((kk + 1) >> 1) & 1);
         }
         return;
       }
@@ -338,82 +356,88 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
             yp2[e] = fma2(Cp[e], hh, yp2[e]);
           }
         }
-        const float yp[4] = {yp2[0].x, yp2[0].y, yp2[1].x, yp2[1].y};
-        // sum the kLPC lanes of a channel (reduce-scatter: lane q keeps the
-        // steps it will store)
-        if constexpr (kLPC == 4) {
-          const bool hi2 = (q & 2) != 0;
-          const float s0 = hi2 ? yp[0] : yp[2], s1 = hi2 ? yp[1] : yp[3];
-          float k0 = hi2 ? yp[2] : yp[0], k1 = hi2 ? yp[3] : yp[1];
-          k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-          k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-          const bool hi1 = (q & 1) != 0;
-          const float sx = hi1 ? k0 : k1;
-          float kk = hi1 ? k1 : k0;
-          kk += __shfl_xor_sync(0xffffffffu, sx, 1);
-          sh.ys[cl][tt + q] += kk;  // step tt + q
-        } else if constexpr (kLPC == 2) {
-          const bool hi = (q & 1) != 0;
-          const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
-          float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
-          k0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-          k1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-          sh.ys[cl][tt + 2 * q] += k0;
-          sh.ys[cl][tt + 2 * q + 1] += k1;
+        if constexpr (kEnd) {
+          dsum += (dl4.x + dl4.y) + (dl4.z + dl4.w);
         } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] += yp[e];
-        }
-        // carry after these 4 steps (entries past the valid length are not
-        // written: the backward never reads them)
-        if (lane_active) {
-          if constexpr (kS == 4) {
-            *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
+          const float yp[4] = {yp2[0].x, yp2[0].y, yp2[1].x, yp2[1].y};
+          // sum the kLPC lanes of a channel (reduce-scatter: lane q keeps the
+          // steps it will store)
+          if constexpr (kLPC == 4) {
+            const bool hi2 = (q & 2) != 0;
+            const float s0 = hi2 ? yp[0] : yp[2], s1 = hi2 ? yp[1] : yp[3];
+            float k0 = hi2 ? yp[2] : yp[0], k1 = hi2 ? yp[3] : yp[1];
+            k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+            k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+            const bool hi1 = (q & 1) != 0;
+            const float sx = hi1 ? k0 : k1;
+            float kk = hi1 ? k1 : k0;
+            kk += __shfl_xor_sync(0xffffffffu, sx, 1);
+            sh.ys[cl][tt + q] += kk;  // step tt + q
+          } else if constexpr (kLPC == 2) {
+            const bool hi = (q & 1) != 0;
+            const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
+            float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
+            k0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+            k1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+            sh.ys[cl][tt + 2 * q] += k0;
+            sh.ys[cl][tt + 2 * q + 1] += k1;
           } else {
 #pragma unroll
-            for (int j = 0; j < kS; ++j) cs[j] = h[j];
+            for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] += yp[e];
           }
+          // carry after these 4 steps (entries past the valid length are not
+          // written: the backward never reads them)
+          if (lane_active) {
+            if constexpr (kS == 4) {
+              *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < kS; ++j) cs[j] = h[j];
+            }
+          }
+          cs += cs_step;
         }
-        cs += cs_step;
       }
     }
 
     __syncthreads();
 
-    // ---- 3. emit out = (y + D u) * silu(z), and y + D u, 4 steps per item
-    for (int i = tid; i < kCh * (kTile / 4); i += kThreads) {
-      const int c = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
-      const int t = t0 + tt;
-      if (c >= n_ch || t >= L) continue;
-      const size_t off = static_cast<size_t>(d0 + c) * L + t;
-      float o[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f};
-      if (t < len) {
-        float zv[4];
-        if (z_b) {
-          if (use_tma) {
-            load4_smem(&sh.rawZ[s][c][tt], zv);
-          } else {
+    if constexpr (!kEnd) {
+      // ---- 3. emit out = (y + D u) * silu(z), and y + D u, 4 steps per item
+      for (int i = tid; i < kCh * (kTile / 4); i += kThreads) {
+        const int c = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
+        const int t = t0 + tt;
+        if (c >= n_ch || t >= L) continue;
+        const size_t off = static_cast<size_t>(d0 + c) * L + t;
+        float o[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f};
+        if (t < len) {
+          float zv[4];
+          if (z_b) {
+            if (use_tma) {
+              load4_smem(&sh.rawZ[s][c][tt], zv);
+            } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+              for (int e = 0; e < 4; ++e) zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (t + e < len) {
+              pre[e] = sh.ys[c][tt + e];
+              o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
+            }
           }
         }
+        if (use_tma) {  // whole, aligned groups: L is a multiple of 4 here
+          store4_global(out_b + off, o);
+          if (pre_b) store4_global(pre_b + off, pre);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (t + e < len) {
-            pre[e] = sh.ys[c][tt + e];
-            o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
-          }
-        }
-      }
-      if (use_tma) {  // whole, aligned groups: L is a multiple of 4 here
-        store4_global(out_b + off, o);
-        if (pre_b) store4_global(pre_b + off, pre);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (t + e < L) {
-            Elem<T>::st(out_b + off + e, o[e]);
-            if (pre_b) Elem<T>::st(pre_b + off + e, pre[e]);
+          for (int e = 0; e < 4; ++e) {
+            if (t + e < L) {
+              Elem<T>::st(out_b + off + e, o[e]);
+              if (pre_b) Elem<T>::st(pre_b + off + e, pre[e]);
+            }
           }
         }
       }
@@ -421,9 +445,42 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
     __syncthreads();
   }
 
-  if (p.last_state && lane_active) {
+  if constexpr (kEnd) {
+    if (lane_active) {
+#pragma unroll
+      for (int j = 0; j < kS; ++j) p.seg_end[seg_row * NS + st_of(j)] = h[j];
+      if (q == 0) p.seg_dsum[seg_row] = dsum;
+    }
+  } else if (p.last_state && lane_active && seg == p.n_seg - 1) {
 #pragma unroll
     for (int j = 0; j < kS; ++j) p.last_state[row * NS + st_of(j)] = h[j];
+  }
+}
+
+// Entering state of every time segment, in order: segment 0 starts from h0
+// (or zero), segment s + 1 from a_seg(s) * in(s) + end(s), where end(s) is
+// segment s's end state from a zero start and a_seg(s) = 2^(A log2 e *
+// sum of delta_eff over s) its decay. One thread per (batch, channel, state).
+__global__ void seg_combine_fwd_kernel(const float* __restrict__ A, const float* __restrict__ h0,
+                                       float* seg_end, float* seg_dsum, float* seg_in,
+                                       int batch, int dim, int dstate, int n_seg) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<long long>(batch) * dim * dstate) return;
+  const int n = static_cast<int>(i % dstate);
+  const long long bd = i / dstate;
+  const int d = static_cast<int>(bd % dim);
+  const float a2 = A[static_cast<size_t>(d) * dstate + n] * kLog2e;
+  float h = h0 ? h0[i] : 0.f;
+  for (int s = 0; s < n_seg; ++s) {
+    const size_t sr = static_cast<size_t>(bd) * n_seg + s;
+    seg_in[sr * dstate + n] = h;
+    if (s + 1 < n_seg) {
+      h = fmaf(exp2f(a2 * seg_dsum[sr]), h, seg_end[sr * dstate + n]);
+    } else {
+      // the last segment has no end-state pass: keep its slots defined
+      seg_end[sr * dstate + n] = 0.f;
+      if (n == 0) seg_dsum[sr] = 0.f;
+    }
   }
 }
 
@@ -432,12 +489,23 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps,
                                 cudaStream_t stream) {
   using Cfg = FwdCfg<NS>;
   const size_t smem = sizeof(FwdShared<NS, T>);
-  auto kern = ss_fwd_kernel<NS, T, kZOH>;
+  auto kern = ss_fwd_kernel<NS, T, kZOH, false>;
+  auto kern_end = ss_fwd_kernel<NS, T, kZOH, true>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  dim3 grid((p.dim + Cfg::kCh - 1) / Cfg::kCh, p.batch);
-  kern<<<grid, Cfg::kThreads, smem, stream>>>(p, maps);
+  const unsigned gx = (p.dim + Cfg::kCh - 1) / Cfg::kCh;
+  if (p.n_seg > 1) {
+    e = cudaFuncSetAttribute(kern_end, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kern_end<<<dim3(gx, p.batch, p.n_seg - 1), Cfg::kThreads, smem, stream>>>(p, maps);
+    const long long total = static_cast<long long>(p.batch) * p.dim * NS;
+    seg_combine_fwd_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        p.A, p.h0, p.seg_end, p.seg_dsum, const_cast<float*>(p.seg_in), p.batch, p.dim, NS,
+        p.n_seg);
+  }
+  kern<<<dim3(gx, p.batch, p.n_seg), Cfg::kThreads, smem, stream>>>(p, maps);
   return cudaPeekAtLastError();
 }
 
@@ -463,6 +531,9 @@ static int fwd_channels_per_cta(int dstate) {
     default: return FwdCfg<16>::kCh;
   }
 }
+static_assert(FwdCfg<16>::kCh == 8 && FwdCfg<8>::kCh == 16 && FwdCfg<4>::kCh == 32 &&
+                  FwdCfg<2>::kCh == 32 && FwdCfg<1>::kCh == 32 && kTile == kScanTile,
+              "seg_plan's CTA count");
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -502,6 +573,17 @@ cudaError_t launch_fwd(const FwdParams& p_in, int dstate, int io_dtype, int zoh,
                        cudaStream_t stream) {
   FwdParams p = p_in;
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
+  // time segments; their scratch follows the carries in chunk_states
+  const SegPlan sp = seg_plan(p.batch, p.seqlen, p.dim, dstate);
+  p.n_seg = sp.n_seg;
+  p.seg_tiles = sp.seg_tiles;
+  if (p.n_seg > 1) {
+    const size_t bds = static_cast<size_t>(p.batch) * p.dim * p.n_seg;
+    float* scratch = p.chunk_states + static_cast<size_t>(p.batch) * p.n_chunks * p.dim * dstate;
+    p.seg_end = scratch;
+    p.seg_in = scratch + bds * dstate;
+    p.seg_dsum = scratch + 2 * bds * dstate;
+  }
   // TMA needs 16-byte aligned bases and row strides (L * esize).
   p.tma_ok = (p.seqlen * esize) % 16 == 0 && aligned16(p.u) && aligned16(p.delta) &&
              aligned16(p.B) && aligned16(p.C) && (!p.z || aligned16(p.z));

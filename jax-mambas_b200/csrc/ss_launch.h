@@ -10,6 +10,31 @@
 
 namespace mss {
 
+// Steps per tile of both scan kernels.
+constexpr int kScanTile = 32;
+
+// Channels per CTA of both scan kernels (8 for N = 16).
+inline int scan_channels_per_cta(int dstate) {
+  const int s = dstate < 4 ? dstate : 4;  // states per lane
+  const int cpw = 32 / (dstate / s);      // channels per warp
+  return cpw < 8 ? 8 : cpw;
+}
+
+// Time segments of a scan: when a problem has too few (batch, channel-block)
+// CTAs to fill the GPU (a single long sequence), L is cut into n_seg segments
+// of seg_tiles tiles that run in parallel; a light pass finds each segment's
+// entering state (forward) or adjoint (backward) first. The environment
+// variable MAMBA_SS_SEGMENTS forces a segment count (tests).
+struct SegPlan {
+  int n_seg;      // >= 1
+  int seg_tiles;  // tiles per segment (the last may be shorter)
+};
+SegPlan seg_plan(int batch, int length, int dim, int dstate);
+
+// fp32 elements of the segment scratch the forward keeps after the carries
+// in chunk_states (0 when n_seg == 1).
+size_t fwd_seg_scratch_elems(int batch, int length, int dim, int dstate);
+
 cudaError_t launch_fwd(const FwdParams& p, int dstate, int io_dtype, int zoh,
                        cudaStream_t stream);
 
