@@ -137,6 +137,20 @@ def _algorithmic(cfg, esize, d=None):
     return elems, fwd, bwd, carry, mufu_fwd, mufu_bwd
 
 
+class _stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration of the block."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self._saved = os.dup(1)
+        os.dup2(2, 1)
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self._saved, 1)
+        os.close(self._saved)
+
+
 def run_gpu(args, cfg):
     import torch
     import torch.distributed as dist
@@ -151,7 +165,11 @@ def run_gpu(args, cfg):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        # NCCL prints its version banner on stdout when the communicator is
+        # created; keep stdout for the one JSON line
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", device_id=dev)
+            dist.barrier()
 
     b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
     chan = cfg.get("shard") == "channels"
