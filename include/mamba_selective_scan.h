@@ -152,6 +152,37 @@ mss_status mamba_ss_fused_step(void* stream, int32_t io_dtype, int32_t discretiz
                                const float* delta_bias, int32_t delta_softplus, void* out);
 
 /* ---------------------------------------------------------------------------
+ * Causal depthwise conv1d + bias + SiLU + padding mask: the operation between
+ * the input projection and the scan in Mamba.__call__ (mamba/mamba1.py:
+ * 313-329: projed *= mask; silu(nnx.Conv(feature_group_count = d_inner,
+ * padding = CAUSAL)(cache ++ projed)) * mask; the conv at mamba1.py:250-255).
+ * Pure JAX / flax in the reference, no FFI counterpart.
+ *
+ * x, u, du, dx: (batch, dim, length) in io_dtype (the scan's layout);
+ * weight, dweight: (kwidth, dim) fp32 (flax's (kwidth, 1, dim) kernel);
+ * bias, dbias: (dim) fp32 or NULL; seq_lens: (batch) or NULL (steps at or past
+ * a sequence's length are masked: inputs read as 0, outputs written as 0);
+ * conv_state, final_state, dconv_state: (batch, dim, kwidth - 1) in io_dtype
+ * or NULL: the kwidth - 1 (masked) inputs before t = 0 (the reference's conv
+ * cache, time-major there), the last kwidth - 1 masked inputs after this
+ * call, and the gradient of conv_state. 1 <= kwidth <= 4.
+ * ------------------------------------------------------------------------- */
+size_t mamba_ss_conv1d_bwd_workspace_bytes(int32_t batch, int32_t dim, int32_t kwidth);
+
+mss_status mamba_ss_conv1d_fwd(void* stream, int32_t io_dtype, int32_t batch, int32_t length,
+                               int32_t dim, int32_t kwidth, const void* x,
+                               const float* weight, const float* bias,
+                               const int32_t* seq_lens, const void* conv_state, void* u,
+                               void* final_state);
+
+mss_status mamba_ss_conv1d_bwd(void* stream, int32_t io_dtype, int32_t batch, int32_t length,
+                               int32_t dim, int32_t kwidth, const void* x,
+                               const float* weight, const float* bias,
+                               const int32_t* seq_lens, const void* conv_state,
+                               const void* du, void* dx, float* dweight, float* dbias,
+                               void* dconv_state, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Allocation-free backward. No counterpart in the reference.
  *
  * For callers that cannot allocate device memory (a host runtime that owns

@@ -353,4 +353,89 @@ mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
                             nullptr, dinitial_x, workspace, workspace_bytes);
 }
 
+size_t mamba_ss_conv1d_bwd_workspace_bytes(int32_t batch, int32_t dim, int32_t kwidth) {
+  if (batch <= 0 || dim <= 0 || kwidth <= 0) return 0;
+  const size_t bd = static_cast<size_t>(batch) * dim;
+  return align256(sizeof(float) * bd * kwidth) + align256(sizeof(float) * bd);
+}
+
+static mss_status check_conv(const char* op, int32_t io_dtype, int32_t batch, int32_t length,
+                             int32_t dim, int32_t kwidth) {
+  if (io_dtype != MSS_F32 && io_dtype != MSS_BF16)
+    return fail(MSS_INVALID_ARGUMENT, std::string(op) + ": io_dtype must be 0 (f32) or 1 (bf16)");
+  if (batch <= 0 || length <= 0 || dim <= 0)
+    return fail(MSS_INVALID_ARGUMENT, std::string(op) + ": batch, length and dim must be positive");
+  if (kwidth < 1 || kwidth > 4)
+    return fail(MSS_INVALID_ARGUMENT, std::string(op) + ": kwidth must be 1 .. 4");
+  if (static_cast<int64_t>(batch) * dim >= (1ll << 31))
+    return fail(MSS_INVALID_ARGUMENT, std::string(op) + ": sizes too large");
+  return MSS_OK;
+}
+
+mss_status mamba_ss_conv1d_fwd(void* stream, int32_t io_dtype, int32_t batch, int32_t length,
+                               int32_t dim, int32_t kwidth, const void* x,
+                               const float* weight, const float* bias,
+                               const int32_t* seq_lens, const void* conv_state, void* u,
+                               void* final_state) {
+  mss_status st = check_conv("mamba_ss_conv1d_fwd", io_dtype, batch, length, dim, kwidth);
+  if (st != MSS_OK) return st;
+  if (!x || !weight || !u)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_conv1d_fwd: x, weight and u must be non-null");
+  mss::ConvParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.seqlen = length;
+  p.x = x;
+  p.weight = weight;
+  p.bias = bias;
+  p.seq_lens = seq_lens;
+  p.state_in = kwidth > 1 ? conv_state : nullptr;
+  p.u = u;
+  p.state_out = kwidth > 1 ? final_state : nullptr;
+  cudaError_t e = mss::launch_conv(p, kwidth, io_dtype, false, nullptr, nullptr,
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching causal conv1d forward", e);
+  return MSS_OK;
+}
+
+mss_status mamba_ss_conv1d_bwd(void* stream, int32_t io_dtype, int32_t batch, int32_t length,
+                               int32_t dim, int32_t kwidth, const void* x,
+                               const float* weight, const float* bias,
+                               const int32_t* seq_lens, const void* conv_state,
+                               const void* du, void* dx, float* dweight, float* dbias,
+                               void* dconv_state, void* workspace, size_t workspace_bytes) {
+  mss_status st = check_conv("mamba_ss_conv1d_bwd", io_dtype, batch, length, dim, kwidth);
+  if (st != MSS_OK) return st;
+  if (!x || !weight || !du || !dx || !dweight)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_conv1d_bwd: x, weight, du, dx and dweight must be non-null");
+  const size_t need = mamba_ss_conv1d_bwd_workspace_bytes(batch, dim, kwidth);
+  if (!workspace || workspace_bytes < need)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_conv1d_bwd: workspace needs " +
+                                          std::to_string(need) + " bytes, got " +
+                                          std::to_string(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_conv1d_bwd: workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  mss::ConvParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.seqlen = length;
+  p.x = x;
+  p.weight = weight;
+  p.bias = bias;
+  p.seq_lens = seq_lens;
+  p.state_in = kwidth > 1 ? conv_state : nullptr;
+  p.du = du;
+  p.dx = dx;
+  p.dstate_in = kwidth > 1 ? dconv_state : nullptr;
+  p.dw_part = reinterpret_cast<float*>(ws);
+  p.db_part = reinterpret_cast<float*>(
+      ws + align256(sizeof(float) * static_cast<size_t>(batch) * dim * kwidth));
+  cudaError_t e = mss::launch_conv(p, kwidth, io_dtype, true, dweight, bias ? dbias : nullptr,
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching causal conv1d backward", e);
+  return MSS_OK;
+}
+
 }  // extern "C"

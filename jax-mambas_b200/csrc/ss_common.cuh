@@ -104,6 +104,25 @@ struct BwdParams {
   float* seg_carry;
 };
 
+// Causal depthwise conv1d + SiLU (ss_conv.cu); rows are (batch, dim) in the
+// scan's (batch, dim, L) layout.
+struct ConvParams {
+  int batch, dim, seqlen;
+  int vec;                 // 4-step vector accesses allowed (set by the launcher)
+  const void* x;           // (batch, dim, L)
+  const float* weight;     // (kwidth, dim)
+  const float* bias;       // (dim) or null
+  const int32_t* seq_lens;
+  const void* state_in;    // (batch, dim, kwidth - 1) or null: inputs before t = 0
+  void* u;                 // forward: (batch, dim, L)
+  void* state_out;         // forward: (batch, dim, kwidth - 1) or null
+  const void* du;          // backward: gradient of u
+  void* dx;                // backward: gradient of x
+  void* dstate_in;         // backward: gradient of state_in, or null
+  float* dw_part;          // backward: (batch, kwidth, dim) partial sums
+  float* db_part;          // backward: (batch, dim)
+};
+
 struct StepParams {
   int batch, dim;
   int delta_softplus;
@@ -291,5 +310,11 @@ __device__ __forceinline__ void add_xor4(float4& acc, const float4& v, int m) {
   acc = make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 __device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
+
+__device__ __forceinline__ float warp_sum32(float v) {
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+  return v;
+}
 
 }  // namespace mss

@@ -46,6 +46,11 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream);
 
+// Causal conv1d + SiLU forward, or backward (then also the batch reduction
+// of dweight / dbias from p.dw_part / p.db_part).
+cudaError_t launch_conv(const ConvParams& p, int kwidth, int io_dtype, bool backward,
+                        float* dweight, float* dbias, cudaStream_t stream);
+
 cudaError_t launch_step(const StepParams& p, int dstate, int io_dtype, int zoh,
                         cudaStream_t stream);
 

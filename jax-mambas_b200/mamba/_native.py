@@ -62,6 +62,18 @@ SIGNATURES = {
         + [_c_void_p] * 8  # state u delta A B C D z
         + [_c_void_p, _i32, _c_void_p],  # delta_bias delta_softplus out
     ),
+    "mamba_ss_conv1d_bwd_workspace_bytes": (ctypes.c_size_t, [_i32, _i32, _i32]),
+    "mamba_ss_conv1d_fwd": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i32, _i32]
+        + [_c_void_p] * 7,  # x weight bias seq_lens conv_state u final_state
+    ),
+    "mamba_ss_conv1d_bwd": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i32, _i32]
+        + [_c_void_p] * 11  # x weight bias seq_lens conv_state du dx dweight dbias dconv_state workspace
+        + [ctypes.c_size_t],
+    ),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,

@@ -18,6 +18,11 @@ It restates, in NumPy, the math of the JAX-Mambas reference:
 * ``fused_backward`` is the analytic adjoint of ``fused_forward`` (the
   reference gets it from ``jax.vjp``, ``mamba/selective_scan_cuda.py:255``);
   the CPU tests pin it against torch.autograd in float64.
+* ``causal_conv1d_forward`` / ``causal_conv1d_backward`` restate the conv
+  step of ``Mamba.__call__`` (``mamba/mamba1.py:313-329`` with the conv of
+  ``mamba1.py:250-255``: mask, causal depthwise flax conv over
+  ``cache ++ projed``, silu, mask) and its adjoint; the CPU tests pin them
+  against torch's grouped conv1d under autograd in float64.
 
 Parity pinning: the reference ships no golden vectors and cannot run here
 (JAX is not installed on this image or on the GPU box). The oracle is pinned
@@ -269,6 +274,59 @@ def fused_step(state, u, delta, A, B, C, D=None, z=None, delta_bias=None,
     if z is not None:
         y = y * z * _sigmoid(z)
     return y, h
+
+
+# --------------------------------------------------------------------------
+# Causal depthwise conv1d + SiLU of the Mamba block, (B, D, L) layout.
+# --------------------------------------------------------------------------
+def _conv_prepare(x, weight, bias, seq_lens, conv_state, dtype):
+    x = np.asarray(x, dtype=dtype)
+    Bn, Dn, L = x.shape
+    K = weight.shape[0]
+    mask = np.ones((Bn, 1, L), dtype=dtype)
+    if seq_lens is not None:
+        mask = (np.arange(L)[None, None, :] < np.asarray(seq_lens)[:, None, None]).astype(dtype)
+    prev = (np.zeros((Bn, Dn, K - 1), dtype=dtype) if conv_state is None
+            else np.asarray(conv_state, dtype=dtype))
+    # projed *= padding_mask; conv input = cache ++ projed (mamba1.py:308-322)
+    xc = np.concatenate([prev, x * mask], axis=2)
+    w = np.asarray(weight, dtype=dtype)
+    pre = np.zeros_like(x) if bias is None else np.broadcast_to(
+        np.asarray(bias, dtype=dtype)[None, :, None], x.shape).copy()
+    # flax CAUSAL conv: out[t] = sum_k w[k] * in[t - (K-1) + k]
+    for k in range(K):
+        pre = pre + w[k][None, :, None] * xc[:, :, k:k + L]
+    return x, mask, xc, pre
+
+
+def causal_conv1d_forward(x, weight, bias=None, seq_lens=None, conv_state=None,
+                          dtype=np.float64):
+    """u = mask * silu(conv(cache ++ mask * x) + bias), the new conv state
+    (the last K - 1 conv inputs) and the pre-activation; x (B, D, L), weight
+    (K, D) (flax's (K, 1, D) kernel), conv_state (B, D, K - 1)."""
+    x, mask, xc, pre = _conv_prepare(x, weight, bias, seq_lens, conv_state, dtype)
+    K = weight.shape[0]
+    u = pre * _sigmoid(pre) * mask  # silu, then conved *= padding_mask
+    final = xc[:, :, xc.shape[2] - (K - 1):]
+    return u, final
+
+
+def causal_conv1d_backward(x, weight, bias, seq_lens, conv_state, du, dtype=np.float64):
+    """Adjoint of causal_conv1d_forward for the cotangent du of u:
+    (dx, dweight (K, D), dbias (D,), dconv_state (B, D, K - 1))."""
+    x, mask, xc, pre = _conv_prepare(x, weight, bias, seq_lens, conv_state, dtype)
+    K = weight.shape[0]
+    L = x.shape[2]
+    s = _sigmoid(pre)
+    g = np.asarray(du, dtype=dtype) * mask * s * (1.0 + pre * (1.0 - s))
+    w = np.asarray(weight, dtype=dtype)
+    dxc = np.zeros_like(xc)
+    dweight = np.zeros_like(w)
+    for k in range(K):
+        dxc[:, :, k:k + L] += w[k][None, :, None] * g
+        dweight[k] = np.sum(g * xc[:, :, k:k + L], axis=(0, 2))
+    dx = dxc[:, :, K - 1:] * mask
+    return dx, dweight, g.sum(axis=(0, 2)), dxc[:, :, :K - 1]
 
 
 # --------------------------------------------------------------------------

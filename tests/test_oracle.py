@@ -129,3 +129,40 @@ def orc_checksum(x):
     return np.array([float(np.asarray(x[k], dtype=np.float64).sum())
                      for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias",
                                "initial_state", "dout")])
+
+
+@pytest.mark.parametrize("kwidth", [1, 2, 3, 4])
+@pytest.mark.parametrize("padded", [False, True])
+def test_conv1d_oracle_matches_torch_autograd(kwidth, padded):
+    """The conv oracle (flax CAUSAL depthwise conv of mamba/mamba1.py:250-255
+    over cache ++ masked input, silu, mask) against torch's grouped conv1d
+    with left padding, differentiated by autograd in float64."""
+    rng = np.random.default_rng(kwidth * 10 + padded)
+    Bn, Dn, L = 3, 5, 23
+    x = rng.standard_normal((Bn, Dn, L))
+    w = rng.standard_normal((kwidth, Dn))
+    b = rng.standard_normal(Dn)
+    state = rng.standard_normal((Bn, Dn, kwidth - 1))
+    seq = np.array([23, 7, 1], dtype=np.int32) if padded else None
+    du = rng.standard_normal((Bn, Dn, L))
+    u, final = orc.causal_conv1d_forward(x, w, b, seq, state)
+    dx, dw, db, dstate = orc.causal_conv1d_backward(x, w, b, seq, state, du)
+
+    tx = torch.tensor(x, requires_grad=True)
+    tw = torch.tensor(w, requires_grad=True)
+    tb = torch.tensor(b, requires_grad=True)
+    ts = torch.tensor(state, requires_grad=True)
+    mask = torch.ones(Bn, 1, L, dtype=torch.float64)
+    if padded:
+        mask = (torch.arange(L)[None, None, :] < torch.tensor(seq)[:, None, None]).double()
+    xc = torch.cat([ts, tx * mask], dim=2)
+    # torch conv1d is a cross-correlation with weight (D, 1, K): same taps
+    pre = torch.nn.functional.conv1d(xc, tw.t().unsqueeze(1), tb, groups=Dn)
+    tu = torch.nn.functional.silu(pre) * mask
+    (tu * torch.tensor(du)).sum().backward()
+    np.testing.assert_allclose(u, tu.detach().numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(final, xc[:, :, L:].detach().numpy(), rtol=0, atol=0)
+    np.testing.assert_allclose(dx, tx.grad.numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(dw, tw.grad.numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(db, tb.grad.numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(dstate, ts.grad.numpy(), rtol=1e-12, atol=1e-12)
