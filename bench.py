@@ -477,6 +477,65 @@ def run_step_bench(args):
         "gpu_launches": steps}), flush=True)
 
 
+def run_conv_bench(args):
+    """--config conv: the Mamba block's causal conv1d + SiLU (kernel width 4)
+    forward + backward at the configs[1] shape (B=8, D=1536, L=2048, fp32),
+    one step = mamba_ss_conv1d_fwd + mamba_ss_conv1d_bwd. HBM-bound:
+    algorithmic bytes per element are x read + u written (forward) and x, du
+    read + dx written (backward), 20 B in fp32."""
+    import torch
+
+    from mamba.causal_conv1d import _workspace, conv1d_backward_into, conv1d_forward_into
+
+    dev = torch.device("cuda", 0)
+    b, d, L, k = 8, 1536, 2048, 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    x = torch.randn(b, d, L, generator=g, device=dev)
+    du = torch.randn(b, d, L, generator=g, device=dev)
+    w = torch.randn(k, d, generator=g, device=dev) * 0.5
+    bias = torch.randn(d, generator=g, device=dev)
+    u, dx = torch.empty_like(x), torch.empty_like(x)
+    dw, db = torch.empty_like(w), torch.empty_like(bias)
+    ws = _workspace(b, d, k, dev)
+
+    def step():
+        conv1d_forward_into(x, w, bias, None, None, u)
+        conv1d_backward_into(x, w, bias, None, None, du, dx, dw, db, None, ws)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    with sampler:
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    elems = b * d * L
+    nbytes = elems * 4 * 5
+    hbm, _, src = _peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "causal conv1d + SiLU fwd+bwd B*D*L elements/s", "unit": "Gelem/s",
+        "value": round(elems / (ms * 1e-3) / 1e9, 3), "ms_per_step": round(ms, 4),
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "n_gpus": 1,
+        "config": {"workload": "Mamba block conv step (kernel width 4) at the Mamba-130M "
+                               "layer shape", "batch": b, "dim": d, "length": L, "kwidth": k,
+                   "l2": f"inputs larger than L2 ({elems * 4 * 2 / 1e6:.0f} MB read per step)"},
+        "roofline": {"bound": "hbm", "kernel": "ss_conv_fwd_kernel + ss_conv_bwd_kernel",
+                     "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_source": src,
+                     "algorithmic_bytes_per_step": nbytes},
+        "clocks": sampler.summary(),
+        "gpu_launches": args.steps * 3}), flush=True)
+
+
 # ---------------------------------------------------------------- CPU arm
 def _cpu_sample_shape(cfg, seconds_target):
     # a bounded sample: full length and state size, a slice of the channels
@@ -559,7 +618,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["step"], default="c1")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["step", "conv"], default="c1")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -568,12 +627,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.config == "step":
+    if args.config in ("step", "conv"):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the decode-step leg has no "
+            print(json.dumps({"impl": "reference", "unavailable": f"the {args.config} leg has no "
                               "CPU reference arm; see --config c1"}))
         else:
-            run_step_bench(args)
+            (run_step_bench if args.config == "step" else run_conv_bench)(args)
         return
     cfg = CONFIGS[args.config]
     if args.impl == "reference":

@@ -182,6 +182,14 @@ mss_status mamba_ss_conv1d_bwd(void* stream, int32_t io_dtype, int32_t batch, in
                                const void* du, void* dx, float* dweight, float* dbias,
                                void* dconv_state, void* workspace, size_t workspace_bytes);
 
+/* One decode token of the conv (Mamba.step, mamba/mamba1.py:339-355):
+ * x, u (batch, dim); conv_state (batch, dim, kwidth - 1) holds the last
+ * kwidth - 1 inputs and is shifted in place (the reference's cache update,
+ * mamba1.py:351-352); u = silu(bias + sum_k weight[k] * (conv_state ++ x)[k]). */
+mss_status mamba_ss_conv1d_step(void* stream, int32_t io_dtype, int32_t batch, int32_t dim,
+                                int32_t kwidth, const void* x, const float* weight,
+                                const float* bias, void* conv_state, void* u);
+
 /* ---------------------------------------------------------------------------
  * Allocation-free backward. No counterpart in the reference.
  *

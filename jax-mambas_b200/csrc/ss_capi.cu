@@ -438,4 +438,26 @@ mss_status mamba_ss_conv1d_bwd(void* stream, int32_t io_dtype, int32_t batch, in
   return MSS_OK;
 }
 
+mss_status mamba_ss_conv1d_step(void* stream, int32_t io_dtype, int32_t batch, int32_t dim,
+                                int32_t kwidth, const void* x, const float* weight,
+                                const float* bias, void* conv_state, void* u) {
+  mss_status st = check_conv("mamba_ss_conv1d_step", io_dtype, batch, 1, dim, kwidth);
+  if (st != MSS_OK) return st;
+  if (!x || !weight || !u || (kwidth > 1 && !conv_state))
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_conv1d_step: x, weight, u and (kwidth > 1) conv_state must be non-null");
+  mss::ConvParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.seqlen = 1;
+  p.x = x;
+  p.weight = weight;
+  p.bias = bias;
+  p.u = u;
+  p.state_out = conv_state;
+  cudaError_t e = mss::launch_conv_step(p, kwidth, io_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching causal conv1d step", e);
+  return MSS_OK;
+}
+
 }  // extern "C"

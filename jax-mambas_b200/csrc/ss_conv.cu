@@ -244,6 +244,47 @@ __global__ void conv_reduce_kernel(const float* __restrict__ dw_part,
   }
 }
 
+// One decode token of the conv (Mamba.step, mamba/mamba1.py:339-355): per
+// (batch, channel), u = silu(bias + sum_k w_k [state, x]_k) over the conv
+// state (the last kwidth - 1 inputs) followed by the new input x, and the
+// state shifts by one (in place). One thread per (batch, channel).
+template <typename T, int K>
+__global__ void __launch_bounds__(256) ss_conv_step_kernel(const ConvParams p) {
+  const long long r = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= static_cast<long long>(p.batch) * p.dim) return;
+  const int d = static_cast<int>(r % p.dim);
+  float win[K];
+  T* st = static_cast<T*>(p.state_out) + r * (K - 1);
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) win[j] = Elem<T>::ld(st + j);
+  win[K - 1] = Elem<T>::ld(static_cast<const T*>(p.x) + r);
+  float acc = p.bias ? __ldg(p.bias + d) : 0.f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) acc = fmaf(__ldg(p.weight + static_cast<size_t>(k) * p.dim + d), win[k], acc);
+  Elem<T>::st(static_cast<T*>(p.u) + r, silu_f(acc));
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) Elem<T>::st(st + j, win[j + 1]);
+}
+
+template <typename T>
+static cudaError_t launch_conv_step_t(const ConvParams& p, int kwidth, cudaStream_t stream) {
+  const long long rows = static_cast<long long>(p.batch) * p.dim;
+  const unsigned grid = static_cast<unsigned>((rows + 255) / 256);
+  switch (kwidth) {
+    case 1: ss_conv_step_kernel<T, 1><<<grid, 256, 0, stream>>>(p); break;
+    case 2: ss_conv_step_kernel<T, 2><<<grid, 256, 0, stream>>>(p); break;
+    case 3: ss_conv_step_kernel<T, 3><<<grid, 256, 0, stream>>>(p); break;
+    case 4: ss_conv_step_kernel<T, 4><<<grid, 256, 0, stream>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_conv_step(const ConvParams& p, int kwidth, int io_dtype, cudaStream_t stream) {
+  if (io_dtype == MSS_BF16) return launch_conv_step_t<__nv_bfloat16>(p, kwidth, stream);
+  return launch_conv_step_t<float>(p, kwidth, stream);
+}
+
 template <typename T>
 static cudaError_t launch_conv_t(const ConvParams& p, int kwidth, bool backward,
                                  float* dweight, float* dbias, cudaStream_t stream) {

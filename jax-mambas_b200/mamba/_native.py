@@ -74,6 +74,10 @@ SIGNATURES = {
         + [_c_void_p] * 11  # x weight bias seq_lens conv_state du dx dweight dbias dconv_state workspace
         + [ctypes.c_size_t],
     ),
+    "mamba_ss_conv1d_step": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i32] + [_c_void_p] * 5,  # x weight bias conv_state u
+    ),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,

@@ -119,3 +119,25 @@ def causal_conv1d_fn(x, weight, bias=None, seq_lens=None, conv_state=None,
     _check(x, weight, bias, seq_lens, conv_state)
     u, final = _CausalConv1d.apply(x, weight, bias, seq_lens, conv_state, return_final_state)
     return (u, final) if return_final_state else u
+
+
+def causal_conv1d_update(x, conv_state, weight, bias=None):
+    """One decode token (Mamba.step, mamba/mamba1.py:339-355): x (B, D) ->
+    u = silu(bias + sum_k weight[k] * (conv_state ++ x)[k]); conv_state
+    (B, D, k-1) is shifted in place. Returns u."""
+    if x.ndim != 2 or not x.is_cuda:
+        raise ValueError("x must be a CUDA tensor of shape (B, D)")
+    batch, dim = x.shape
+    k = weight.shape[0]
+    if weight.shape != (k, dim) or weight.dtype != torch.float32:
+        raise ValueError("weight must be float32 of shape (k, D)")
+    if k > 1 and (conv_state is None or conv_state.shape != (batch, dim, k - 1)
+                  or conv_state.dtype != x.dtype or not conv_state.is_contiguous()):
+        raise ValueError("conv_state must be a contiguous (B, D, k - 1) tensor of x's dtype")
+    x = x.contiguous()
+    u = torch.empty_like(x)
+    lib = _lib()
+    st = lib.mamba_ss_conv1d_step(_stream(x.device), _io_dtype(x), batch, dim, k, _ptr(x),
+                                  _ptr(weight.contiguous()), _ptr(bias), _ptr(conv_state), _ptr(u))
+    _native.check(lib, st)
+    return u

@@ -108,3 +108,23 @@ def test_rejects_bad_arguments():
     with pytest.raises(ValueError):
         conv1d_forward_into(x, w, None, None, None, torch.empty_like(x))
     assert b"kwidth" in _native.load().mamba_ss_last_error()
+
+
+@pytest.mark.parametrize("K", [2, 4])
+@pytest.mark.parametrize("io", [torch.float32, torch.bfloat16])
+def test_decode_steps_match_the_sequence(K, io):
+    """Token-by-token conv steps reproduce the full-sequence conv (the
+    reference's Mamba.step vs Mamba.__call__, mamba/mamba1.py:301-355), and
+    leave the same conv state."""
+    from mamba.causal_conv1d import causal_conv1d_fn, causal_conv1d_update
+
+    x, w, b, _, st, _ = _inputs(3, 10, 9, K, seed=40 + K)
+    tx, tw, tb = to_dev(x, dtype=io), to_dev(w), to_dev(b)
+    tst = to_dev(st, dtype=io)
+    u_seq, final = causal_conv1d_fn(tx, tw, tb, None, tst.clone(), return_final_state=True)
+    state = tst.clone()
+    steps = [causal_conv1d_update(tx[:, :, t], state, tw, tb) for t in range(x.shape[2])]
+    u_step = torch.stack(steps, dim=2)
+    tol = FWD_TOL if io == torch.float32 else BF16_TOL
+    assert_close(u_step.float().cpu().numpy(), u_seq.float().cpu().numpy(), tol, "u")
+    assert torch.equal(state, final)
