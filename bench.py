@@ -497,7 +497,7 @@ def run_conv_bench(args):
     bias = torch.randn(d, generator=g, device=dev)
     u, dx = torch.empty_like(x), torch.empty_like(x)
     dw, db = torch.empty_like(w), torch.empty_like(bias)
-    ws = _workspace(b, d, k, dev)
+    ws = _workspace(b, L, d, k, dev)
 
     def step():
         conv1d_forward_into(x, w, bias, None, None, u)

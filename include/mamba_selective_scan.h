@@ -167,7 +167,8 @@ mss_status mamba_ss_fused_step(void* stream, int32_t io_dtype, int32_t discretiz
  * cache, time-major there), the last kwidth - 1 masked inputs after this
  * call, and the gradient of conv_state. 1 <= kwidth <= 4.
  * ------------------------------------------------------------------------- */
-size_t mamba_ss_conv1d_bwd_workspace_bytes(int32_t batch, int32_t dim, int32_t kwidth);
+size_t mamba_ss_conv1d_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
+                                           int32_t kwidth);
 
 mss_status mamba_ss_conv1d_fwd(void* stream, int32_t io_dtype, int32_t batch, int32_t length,
                                int32_t dim, int32_t kwidth, const void* x,

@@ -353,9 +353,10 @@ mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
                             nullptr, dinitial_x, workspace, workspace_bytes);
 }
 
-size_t mamba_ss_conv1d_bwd_workspace_bytes(int32_t batch, int32_t dim, int32_t kwidth) {
-  if (batch <= 0 || dim <= 0 || kwidth <= 0) return 0;
-  const size_t bd = static_cast<size_t>(batch) * dim;
+size_t mamba_ss_conv1d_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
+                                           int32_t kwidth) {
+  if (batch <= 0 || length <= 0 || dim <= 0 || kwidth <= 0) return 0;
+  const size_t bd = static_cast<size_t>(batch) * mss::conv_segments(length) * dim;
   return align256(sizeof(float) * bd * kwidth) + align256(sizeof(float) * bd);
 }
 
@@ -409,7 +410,7 @@ mss_status mamba_ss_conv1d_bwd(void* stream, int32_t io_dtype, int32_t batch, in
   if (!x || !weight || !du || !dx || !dweight)
     return fail(MSS_INVALID_ARGUMENT,
                 "mamba_ss_conv1d_bwd: x, weight, du, dx and dweight must be non-null");
-  const size_t need = mamba_ss_conv1d_bwd_workspace_bytes(batch, dim, kwidth);
+  const size_t need = mamba_ss_conv1d_bwd_workspace_bytes(batch, length, dim, kwidth);
   if (!workspace || workspace_bytes < need)
     return fail(MSS_INVALID_ARGUMENT, "mamba_ss_conv1d_bwd: workspace needs " +
                                           std::to_string(need) + " bytes, got " +
@@ -431,7 +432,8 @@ mss_status mamba_ss_conv1d_bwd(void* stream, int32_t io_dtype, int32_t batch, in
   p.dstate_in = kwidth > 1 ? dconv_state : nullptr;
   p.dw_part = reinterpret_cast<float*>(ws);
   p.db_part = reinterpret_cast<float*>(
-      ws + align256(sizeof(float) * static_cast<size_t>(batch) * dim * kwidth));
+      ws + align256(sizeof(float) * static_cast<size_t>(batch) * mss::conv_segments(length) *
+                    dim * kwidth));
   cudaError_t e = mss::launch_conv(p, kwidth, io_dtype, true, dweight, bias ? dbias : nullptr,
                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail("launching causal conv1d backward", e);

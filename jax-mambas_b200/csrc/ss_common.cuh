@@ -119,8 +119,8 @@ struct ConvParams {
   const void* du;          // backward: gradient of u
   void* dx;                // backward: gradient of x
   void* dstate_in;         // backward: gradient of state_in, or null
-  float* dw_part;          // backward: (batch, kwidth, dim) partial sums
-  float* db_part;          // backward: (batch, dim)
+  float* dw_part;          // backward: (batch, segments, kwidth, dim) partial sums
+  float* db_part;          // backward: (batch, segments, dim)
 };
 
 struct StepParams {

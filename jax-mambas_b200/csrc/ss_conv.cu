@@ -64,33 +64,60 @@ __device__ __forceinline__ void store4_row(T* row, int t, int L, bool vec, const
   }
 }
 
+// Work units: a warp takes a segment of kConvSegChunks chunks of one row
+// (unit = row * n_seg + segment), so that a layer splits into many equal
+// units (no partial last wave) and each warp has all its loads in flight at
+// once. Pre-segment inputs (forward) and post-segment gradients (backward)
+// are read or recomputed at the segment edges.
+constexpr int kConvSegChunks = 4;
+constexpr int kConvSeg = kConvSegChunks * kConvChunk;  // steps per segment
+
+// masked input t of a row (the conv state before t = 0; 0 before that)
+template <typename T, int K>
+__device__ __forceinline__ float conv_input(const T* xr, const T* sin, int t, int len) {
+  if (t >= 0) return t < len ? Elem<T>::ld(xr + t) : 0.f;
+  return (sin && t >= -(K - 1)) ? Elem<T>::ld(sin + (K - 1) + t) : 0.f;
+}
+
 template <typename T, int K>
 __global__ void __launch_bounds__(128) ss_conv_fwd_kernel(const ConvParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long r = static_cast<long long>(blockIdx.x) * 4 + warp;  // b * dim + d
-  if (r >= static_cast<long long>(p.batch) * p.dim) return;          // warp-uniform
-  const int b = static_cast<int>(r / p.dim), d = static_cast<int>(r % p.dim);
   const int L = p.seqlen;
+  const int n_seg = (L + kConvSeg - 1) / kConvSeg;
+  const long long unit = static_cast<long long>(blockIdx.x) * 4 + warp;
+  if (unit >= static_cast<long long>(p.batch) * p.dim * n_seg) return;  // warp-uniform
+  const long long r = unit / n_seg;  // b * dim + d
+  const int s0 = static_cast<int>(unit % n_seg) * kConvSeg;
+  const int b = static_cast<int>(r / p.dim), d = static_cast<int>(r % p.dim);
   int len = L;
   if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
-  const T* xr = static_cast<const T*>(p.x) + r * L;
-  T* ur = static_cast<T*>(p.u) + r * L;
+  const T* __restrict__ xr = static_cast<const T*>(p.x) + r * L;
+  T* __restrict__ ur = static_cast<T*>(p.u) + r * L;
   const T* sin = p.state_in ? static_cast<const T*>(p.state_in) + r * (K - 1) : nullptr;
   float w[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) w[k] = __ldg(p.weight + static_cast<size_t>(k) * p.dim + d);
   const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
 
-  // masked inputs at t0 - 3, t0 - 2, t0 - 1 (the conv state before t = 0)
-  float c3[3] = {0.f, 0.f, 0.f};
-  if (sin) {
+  // all of the segment's inputs first (independent loads)
+  float xs[kConvSegChunks][4];
 #pragma unroll
-    for (int j = 0; j < K - 1; ++j) c3[3 - (K - 1) + j] = Elem<T>::ld(sin + j);
+  for (int c = 0; c < kConvSegChunks; ++c)
+    load4_row(xr, s0 + c * kConvChunk + lane * 4, len, p.vec != 0, xs[c]);
+  // masked inputs at s0 - 3 .. s0 - 1
+  float c3[3];
+  {
+    const float v = lane < 3 ? conv_input<T, K>(xr, sin, s0 - 3 + lane, len) : 0.f;
+    c3[0] = __shfl_sync(0xffffffffu, v, 0);
+    c3[1] = __shfl_sync(0xffffffffu, v, 1);
+    c3[2] = __shfl_sync(0xffffffffu, v, 2);
   }
-  for (int t0 = 0; t0 < L; t0 += kConvChunk) {
+#pragma unroll
+  for (int c = 0; c < kConvSegChunks; ++c) {
+    const int t0 = s0 + c * kConvChunk;
+    if (t0 >= L) break;  // warp-uniform
     const int t = t0 + lane * 4;
-    float xv[4];
-    load4_row(xr, t, len, p.vec != 0, xv);
+    const float(&xv)[4] = xs[c];
     float p1 = __shfl_up_sync(0xffffffffu, xv[1], 1);
     float p2 = __shfl_up_sync(0xffffffffu, xv[2], 1);
     float p3 = __shfl_up_sync(0xffffffffu, xv[3], 1);
@@ -114,62 +141,89 @@ __global__ void __launch_bounds__(128) ss_conv_fwd_kernel(const ConvParams p) {
     c3[2] = __shfl_sync(0xffffffffu, xv[3], 31);
   }
   // the last kwidth - 1 masked inputs: the conv state of the next call
-  if (p.state_out && lane < K - 1) {
-    const int tt = L - (K - 1) + lane;
-    float v = 0.f;
-    if (tt >= 0)
-      v = tt < len ? Elem<T>::ld(xr + tt) : 0.f;
-    else if (sin)
-      v = Elem<T>::ld(sin + (K - 1) + tt);
-    Elem<T>::st(static_cast<T*>(p.state_out) + r * (K - 1) + lane, v);
-  }
+  if (p.state_out && s0 + kConvSeg >= L && lane < K - 1)
+    Elem<T>::st(static_cast<T*>(p.state_out) + r * (K - 1) + lane,
+                conv_input<T, K>(xr, sin, L - (K - 1) + lane, len));
 }
 
 template <typename T, int K>
 __global__ void __launch_bounds__(128) ss_conv_bwd_kernel(const ConvParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long r = static_cast<long long>(blockIdx.x) * 4 + warp;
-  if (r >= static_cast<long long>(p.batch) * p.dim) return;
-  const int b = static_cast<int>(r / p.dim), d = static_cast<int>(r % p.dim);
   const int L = p.seqlen;
+  const int n_seg = (L + kConvSeg - 1) / kConvSeg;
+  const long long unit = static_cast<long long>(blockIdx.x) * 4 + warp;
+  if (unit >= static_cast<long long>(p.batch) * p.dim * n_seg) return;
+  const long long r = unit / n_seg;
+  const int seg = static_cast<int>(unit % n_seg);
+  const int s0 = seg * kConvSeg, s1 = min(L, s0 + kConvSeg);
+  const int b = static_cast<int>(r / p.dim), d = static_cast<int>(r % p.dim);
   int len = L;
   if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
-  const T* xr = static_cast<const T*>(p.x) + r * L;
-  const T* gr = static_cast<const T*>(p.du) + r * L;
-  T* dxr = static_cast<T*>(p.dx) + r * L;
+  const T* __restrict__ xr = static_cast<const T*>(p.x) + r * L;
+  const T* __restrict__ gr = static_cast<const T*>(p.du) + r * L;
+  T* __restrict__ dxr = static_cast<T*>(p.dx) + r * L;
   const T* sin = p.state_in ? static_cast<const T*>(p.state_in) + r * (K - 1) : nullptr;
   float w[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) w[k] = __ldg(p.weight + static_cast<size_t>(k) * p.dim + d);
   const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
 
-  // gradient of the conv output (before SiLU) at the 3 steps after the chunk
-  float gn[3] = {0.f, 0.f, 0.f};
+  float xs[kConvSegChunks][4], ds[kConvSegChunks][4];
+#pragma unroll
+  for (int c = 0; c < kConvSegChunks; ++c) {
+    const int t = s0 + c * kConvChunk + lane * 4;
+    load4_row(xr, t, len, p.vec != 0, xs[c]);
+    load4_row(gr, t, len, p.vec != 0, ds[c]);
+  }
+  // gradient of the conv output (before SiLU) at s1 .. s1 + 2, recomputed
+  float gn[3];
+  {
+    float v = 0.f;
+    const int t = s1 + lane;
+    if (lane < 3 && t < len) {
+      float acc = bias;
+#pragma unroll
+      for (int k = 0; k < K; ++k)
+        acc = fmaf(w[k], conv_input<T, K>(xr, sin, t - (K - 1) + k, len), acc);
+      v = Elem<T>::ld(gr + t) * dsilu(acc);
+    }
+    gn[0] = __shfl_sync(0xffffffffu, v, 0);
+    gn[1] = __shfl_sync(0xffffffffu, v, 1);
+    gn[2] = __shfl_sync(0xffffffffu, v, 2);
+  }
   float dwp[K], dbp = 0.f;
 #pragma unroll
   for (int k = 0; k < K; ++k) dwp[k] = 0.f;
-  const int n_chunks = (L + kConvChunk - 1) / kConvChunk;
-  for (int ci = n_chunks - 1; ci >= 0; --ci) {
-    const int t0 = ci * kConvChunk;
+#pragma unroll
+  for (int c = kConvSegChunks - 1; c >= 0; --c) {
+    const int t0 = s0 + c * kConvChunk;
+    if (t0 >= L) continue;  // warp-uniform
     const int t = t0 + lane * 4;
-    float xv[4], dv[4];
-    load4_row(xr, t, len, p.vec != 0, xv);
-    load4_row(gr, t, len, p.vec != 0, dv);
+    const float(&xv)[4] = xs[c];
+    const float(&dv)[4] = ds[c];
     float p1 = __shfl_up_sync(0xffffffffu, xv[1], 1);
     float p2 = __shfl_up_sync(0xffffffffu, xv[2], 1);
     float p3 = __shfl_up_sync(0xffffffffu, xv[3], 1);
-    if (lane == 0) {
-      // the three inputs before the chunk (the conv state before t = 0)
-      float q[3];
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int tt = t0 - 3 + j;
-        q[j] = tt >= 0 ? (tt < len ? Elem<T>::ld(xr + tt) : 0.f)
-                       : ((sin && tt >= -(K - 1)) ? Elem<T>::ld(sin + (K - 1) + tt) : 0.f);
+    if (c > 0) {
+      const float q1 = __shfl_sync(0xffffffffu, xs[c > 0 ? c - 1 : 0][1], 31);
+      const float q2 = __shfl_sync(0xffffffffu, xs[c > 0 ? c - 1 : 0][2], 31);
+      const float q3 = __shfl_sync(0xffffffffu, xs[c > 0 ? c - 1 : 0][3], 31);
+      if (lane == 0) {
+        p1 = q1;
+        p2 = q2;
+        p3 = q3;
       }
-      p1 = q[0];
-      p2 = q[1];
-      p3 = q[2];
+    } else {
+      // the three inputs before the segment (the conv state before t = 0)
+      const float v = lane < 3 ? conv_input<T, K>(xr, sin, s0 - 3 + lane, len) : 0.f;
+      const float q1 = __shfl_sync(0xffffffffu, v, 0);
+      const float q2 = __shfl_sync(0xffffffffu, v, 1);
+      const float q3 = __shfl_sync(0xffffffffu, v, 2);
+      if (lane == 0) {
+        p1 = q1;
+        p2 = q2;
+        p3 = q3;
+      }
     }
     const float win[7] = {p1, p2, p3, xv[0], xv[1], xv[2], xv[3]};
     float g[4];
@@ -206,27 +260,27 @@ __global__ void __launch_bounds__(128) ss_conv_bwd_kernel(const ConvParams p) {
     gn[2] = __shfl_sync(0xffffffffu, g[2], 0);
   }
   // gradient of the conv state: input -(K-1)+j feeds the outputs t = j - k
-  if (p.dstate_in && lane < K - 1) {
+  if (seg == 0 && p.dstate_in && lane < K - 1) {
     float acc = 0.f;
 #pragma unroll
     for (int k = 0; k < K; ++k)
-      if (k <= lane) acc = fmaf(w[k], gn[lane - k], acc);
+      if (k <= lane) acc = fmaf(w[k], lane - k == 0 ? gn[0] : lane - k == 1 ? gn[1] : gn[2], acc);
     Elem<T>::st(static_cast<T*>(p.dstate_in) + r * (K - 1) + lane, acc);
   }
-  // per-row partial sums of dweight and dbias
+  // per-(row, segment) partial sums of dweight and dbias
 #pragma unroll
   for (int k = 0; k < K; ++k) dwp[k] = warp_sum32(dwp[k]);
   dbp = warp_sum32(dbp);
   if (lane == 0) {
+    const size_t bs = static_cast<size_t>(b) * n_seg + seg;  // partial row (batch, segment)
 #pragma unroll
-    for (int k = 0; k < K; ++k)
-      p.dw_part[(static_cast<size_t>(b) * K + k) * p.dim + d] = dwp[k];
-    p.db_part[static_cast<size_t>(b) * p.dim + d] = dbp;
+    for (int k = 0; k < K; ++k) p.dw_part[(bs * K + k) * p.dim + d] = dwp[k];
+    p.db_part[bs * p.dim + d] = dbp;
   }
 }
 
-// dweight (kwidth, dim) and dbias (dim) from the per-batch partials, summed in
-// a fixed order.
+// dweight (kwidth, dim) and dbias (dim) from the per-(batch, segment)
+// partials, summed in a fixed order.
 __global__ void conv_reduce_kernel(const float* __restrict__ dw_part,
                                    const float* __restrict__ db_part, float* dweight,
                                    float* dbias, int batch, int dim, int kwidth) {
@@ -288,8 +342,8 @@ cudaError_t launch_conv_step(const ConvParams& p, int kwidth, int io_dtype, cuda
 template <typename T>
 static cudaError_t launch_conv_t(const ConvParams& p, int kwidth, bool backward,
                                  float* dweight, float* dbias, cudaStream_t stream) {
-  const long long rows = static_cast<long long>(p.batch) * p.dim;
-  const dim3 grid(static_cast<unsigned>((rows + 3) / 4));
+  const long long units = static_cast<long long>(p.batch) * p.dim * conv_segments(p.seqlen);
+  const dim3 grid(static_cast<unsigned>((units + 3) / 4));
   switch (kwidth) {
 #define MSS_CONV_CASE(KW)                                                   \
   case KW:                                                                  \
@@ -309,10 +363,12 @@ static cudaError_t launch_conv_t(const ConvParams& p, int kwidth, bool backward,
   cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess || !backward) return e;
   const int total = kwidth * p.dim + p.dim;
-  conv_reduce_kernel<<<(total + 255) / 256, 256, 0, stream>>>(p.dw_part, p.db_part, dweight,
-                                                              dbias, p.batch, p.dim, kwidth);
+  conv_reduce_kernel<<<(total + 255) / 256, 256, 0, stream>>>(
+      p.dw_part, p.db_part, dweight, dbias, p.batch * conv_segments(p.seqlen), p.dim, kwidth);
   return cudaPeekAtLastError();
 }
+
+int conv_segments(int length) { return (length + kConvSeg - 1) / kConvSeg; }
 
 cudaError_t launch_conv(const ConvParams& p_in, int kwidth, int io_dtype, bool backward,
                         float* dweight, float* dbias, cudaStream_t stream) {

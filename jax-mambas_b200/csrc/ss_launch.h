@@ -51,6 +51,10 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
 cudaError_t launch_conv(const ConvParams& p, int kwidth, int io_dtype, bool backward,
                         float* dweight, float* dbias, cudaStream_t stream);
 
+// Segments per row of the conv kernels (their dweight / dbias partials are
+// per (batch, segment)).
+int conv_segments(int length);
+
 // One decode token of the conv: p.x, p.u (batch, dim), p.state_out the conv
 // state (batch, dim, kwidth - 1), shifted in place.
 cudaError_t launch_conv_step(const ConvParams& p, int kwidth, int io_dtype, cudaStream_t stream);

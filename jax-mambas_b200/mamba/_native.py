@@ -62,7 +62,7 @@ SIGNATURES = {
         + [_c_void_p] * 8  # state u delta A B C D z
         + [_c_void_p, _i32, _c_void_p],  # delta_bias delta_softplus out
     ),
-    "mamba_ss_conv1d_bwd_workspace_bytes": (ctypes.c_size_t, [_i32, _i32, _i32]),
+    "mamba_ss_conv1d_bwd_workspace_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
     "mamba_ss_conv1d_fwd": (
         ctypes.c_int,
         [_c_void_p, _i32, _i32, _i32, _i32, _i32]

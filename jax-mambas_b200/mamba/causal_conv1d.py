@@ -22,8 +22,8 @@ from . import _native
 from .selective_scan_cuda import _io_dtype, _lib, _ptr, _stream
 
 
-def conv1d_bwd_workspace_bytes(batch, dim, kwidth):
-    return int(_lib().mamba_ss_conv1d_bwd_workspace_bytes(batch, dim, kwidth))
+def conv1d_bwd_workspace_bytes(batch, length, dim, kwidth):
+    return int(_lib().mamba_ss_conv1d_bwd_workspace_bytes(batch, length, dim, kwidth))
 
 
 def conv1d_forward_into(x, weight, bias, seq_lens, conv_state, u, final_state=None):
@@ -49,8 +49,8 @@ def conv1d_backward_into(x, weight, bias, seq_lens, conv_state, du, dx, dweight,
     _native.check(lib, st)
 
 
-def _workspace(batch, dim, kwidth, device):
-    nbytes = conv1d_bwd_workspace_bytes(batch, dim, kwidth)
+def _workspace(batch, length, dim, kwidth, device):
+    nbytes = conv1d_bwd_workspace_bytes(batch, length, dim, kwidth)
     ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
     off = (-ws.data_ptr()) % 256
     return ws[off:off + nbytes]
@@ -103,7 +103,7 @@ class _CausalConv1d(torch.autograd.Function):
         dbias = torch.empty_like(bias) if bias is not None else None
         dstate = torch.empty_like(conv_state) if conv_state is not None else None
         conv1d_backward_into(x, weight, bias, seq_lens, conv_state, du, dx, dweight, dbias,
-                             dstate, _workspace(batch, dim, k, x.device))
+                             dstate, _workspace(batch, x.shape[2], dim, k, x.device))
         return dx, dweight, dbias, None, dstate, None
 
 
