@@ -152,6 +152,40 @@ mss_status mamba_ss_fused_step(void* stream, int32_t io_dtype, int32_t discretiz
                                const float* delta_bias, int32_t delta_softplus, void* out);
 
 /* ---------------------------------------------------------------------------
+ * Complex SSM (S6 with complex_ssm = True, mamba/mamba1.py:170-176, 196;
+ * pure JAX in the reference, no FFI counterpart): A (dim, dstate), B, C
+ * (batch, dstate, length), initial/last state and its gradient (batch, dim,
+ * dstate) are complex64 (interleaved float pairs); u, delta, z, out, out_pre,
+ * dout and the other gradients are fp32 (batch, dim, length);
+ * out = (Re(C . h) + D u) * silu(z). Gradients of complex arguments are
+ * dL/dRe + i dL/dIm (torch's convention; JAX's cotangent is the conjugate).
+ * chunk_states holds complex carries (mamba_ss_complex_chunk_states_elems
+ * floats); the backward needs mamba_ss_complex_bwd_workspace_bytes of
+ * 256-byte aligned workspace.
+ * ------------------------------------------------------------------------- */
+int64_t mamba_ss_complex_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
+                                            int32_t dstate);
+size_t mamba_ss_complex_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
+                                            int32_t dstate);
+
+mss_status mamba_ss_complex_fwd(void* stream, int32_t discretization, int32_t batch,
+                                int32_t length, int32_t dim, int32_t dstate, const float* u,
+                                const float* delta, const void* A, const void* B, const void* C,
+                                const float* D, const float* z, const float* delta_bias,
+                                int32_t delta_softplus, const void* initial_state,
+                                const int32_t* seq_lens, float* out, float* out_pre,
+                                void* last_state, float* chunk_states);
+
+mss_status mamba_ss_complex_bwd(
+    void* stream, int32_t discretization, int32_t batch, int32_t length, int32_t dim,
+    int32_t dstate, const float* u, const float* delta, const void* A, const void* B,
+    const void* C, const float* D, const float* z, const float* delta_bias,
+    int32_t delta_softplus, const void* initial_state, const int32_t* seq_lens,
+    const float* chunk_states, const float* out_pre, const float* dout, const void* dlast_state,
+    float* du, float* ddelta, void* dA, void* dB, void* dC, float* dD, float* dz,
+    float* ddelta_bias, void* dinitial_state, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Causal depthwise conv1d + bias + SiLU + padding mask: the operation between
  * the input projection and the scan in Mamba.__call__ (mamba/mamba1.py:
  * 313-329: projed *= mask; silu(nnx.Conv(feature_group_count = d_inner,

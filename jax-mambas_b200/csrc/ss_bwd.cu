@@ -962,6 +962,15 @@ __global__ void reduce_params_kernel(const float* __restrict__ dA_part,
   }
 }
 
+cudaError_t launch_param_reduce(const float* dA_part, const float* dD_part,
+                                const float* dbias_part, float* dA, float* dD, float* dbias,
+                                int batch, int dim, int dstate, cudaStream_t stream) {
+  const int total = dim * dstate + 2 * dim;
+  reduce_params_kernel<<<(total + 255) / 256, 256, 0, stream>>>(dA_part, dD_part, dbias_part,
+                                                                dA, dD, dbias, batch, dim, dstate);
+  return cudaPeekAtLastError();
+}
+
 __global__ void f32_to_bf16_kernel(const float* __restrict__ src,
                                    __nv_bfloat16* __restrict__ dst, size_t n) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;

@@ -462,4 +462,126 @@ mss_status mamba_ss_conv1d_step(void* stream, int32_t io_dtype, int32_t batch, i
   return MSS_OK;
 }
 
+int64_t mamba_ss_complex_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
+                                            int32_t dstate) {
+  if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
+  return 2 * static_cast<int64_t>(batch) * dim * n_chunks_of(length) * dstate;
+}
+
+size_t mamba_ss_complex_bwd_workspace_bytes(int32_t batch, int32_t length, int32_t dim,
+                                            int32_t dstate) {
+  if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
+  const size_t bd = static_cast<size_t>(batch) * dim;
+  const size_t bnl = static_cast<size_t>(batch) * dstate * length;
+  return align256(sizeof(float) * bd * dstate * 2) + 2 * align256(sizeof(float) * bd) +
+         4 * align256(sizeof(float) * bnl);
+}
+
+static mss::CplxParams complex_params(int32_t batch, int32_t length, int32_t dim,
+                                      const float* u, const float* delta, const void* A,
+                                      const void* B, const void* C, const float* D,
+                                      const float* z, const float* delta_bias,
+                                      int32_t delta_softplus, const void* initial_state,
+                                      const int32_t* seq_lens) {
+  mss::CplxParams p{};
+  p.batch = batch;
+  p.dim = dim;
+  p.seqlen = length;
+  p.n_chunks = n_chunks_of(length);
+  p.delta_softplus = delta_softplus ? 1 : 0;
+  p.u = u;
+  p.delta = delta;
+  p.z = z;
+  p.A = A;
+  p.B = B;
+  p.C = C;
+  p.D = D;
+  p.delta_bias = delta_bias;
+  p.h0 = initial_state;
+  p.seq_lens = seq_lens;
+  return p;
+}
+
+mss_status mamba_ss_complex_fwd(void* stream, int32_t discretization, int32_t batch,
+                                int32_t length, int32_t dim, int32_t dstate, const float* u,
+                                const float* delta, const void* A, const void* B, const void* C,
+                                const float* D, const float* z, const float* delta_bias,
+                                int32_t delta_softplus, const void* initial_state,
+                                const int32_t* seq_lens, float* out, float* out_pre,
+                                void* last_state, float* chunk_states) {
+  mss_status st = check_dims("mamba_ss_complex_fwd", MSS_F32, discretization, batch, length,
+                             dim, dstate);
+  if (st != MSS_OK) return st;
+  if (!u || !delta || !A || !B || !C || !out || !chunk_states)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_complex_fwd: u, delta, A, B, C, out and chunk_states must be non-null");
+  mss::CplxParams p = complex_params(batch, length, dim, u, delta, A, B, C, D, z, delta_bias,
+                                     delta_softplus, initial_state, seq_lens);
+  p.out = out;
+  p.out_pre = out_pre;
+  p.last_state = last_state;
+  p.chunk_states = chunk_states;
+  cudaError_t e = mss::launch_cplx_fwd(p, dstate, discretization,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching complex selective scan forward", e);
+  return MSS_OK;
+}
+
+mss_status mamba_ss_complex_bwd(
+    void* stream, int32_t discretization, int32_t batch, int32_t length, int32_t dim,
+    int32_t dstate, const float* u, const float* delta, const void* A, const void* B,
+    const void* C, const float* D, const float* z, const float* delta_bias,
+    int32_t delta_softplus, const void* initial_state, const int32_t* seq_lens,
+    const float* chunk_states, const float* out_pre, const float* dout, const void* dlast_state,
+    float* du, float* ddelta, void* dA, void* dB, void* dC, float* dD, float* dz,
+    float* ddelta_bias, void* dinitial_state, void* workspace, size_t workspace_bytes) {
+  mss_status st = check_dims("mamba_ss_complex_bwd", MSS_F32, discretization, batch, length,
+                             dim, dstate);
+  if (st != MSS_OK) return st;
+  if (!u || !delta || !A || !B || !C || !chunk_states || !dout || !du || !ddelta || !dA ||
+      !dB || !dC)
+    return fail(MSS_INVALID_ARGUMENT,
+                "mamba_ss_complex_bwd: u, delta, A, B, C, chunk_states, dout, du, ddelta, dA, "
+                "dB and dC must be non-null");
+  if (z && (!dz || !out_pre))
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_complex_bwd: z given without dz or out_pre");
+  const size_t need = mamba_ss_complex_bwd_workspace_bytes(batch, length, dim, dstate);
+  if (!workspace || workspace_bytes < need)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_complex_bwd: workspace needs " +
+                                          std::to_string(need) + " bytes, got " +
+                                          std::to_string(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(MSS_INVALID_ARGUMENT, "mamba_ss_complex_bwd: workspace must be 256-byte aligned");
+  mss::CplxParams p = complex_params(batch, length, dim, u, delta, A, B, C, D, z, delta_bias,
+                                     delta_softplus, initial_state, seq_lens);
+  p.chunk_states = const_cast<float*>(chunk_states);
+  p.out_pre = const_cast<float*>(out_pre);
+  p.dout = dout;
+  p.dlast = dlast_state;
+  p.du = du;
+  p.ddelta = ddelta;
+  p.dz = z ? dz : nullptr;
+  p.dh0 = dinitial_state;
+  const size_t bd = static_cast<size_t>(batch) * dim;
+  const size_t bnl = static_cast<size_t>(batch) * dstate * length;
+  char* ws = static_cast<char*>(workspace);
+  size_t off = 0;
+  p.dA_part = reinterpret_cast<float*>(ws + off);
+  off += align256(sizeof(float) * bd * dstate * 2);
+  p.dD_part = reinterpret_cast<float*>(ws + off);
+  off += align256(sizeof(float) * bd);
+  p.dbias_part = reinterpret_cast<float*>(ws + off);
+  off += align256(sizeof(float) * bd);
+  float** planes[4] = {&p.dB_acc_r, &p.dB_acc_i, &p.dC_acc_r, &p.dC_acc_i};
+  for (float** pl : planes) {
+    *pl = reinterpret_cast<float*>(ws + off);
+    off += align256(sizeof(float) * bnl);
+  }
+  cudaError_t e = mss::launch_cplx_bwd(p, dstate, discretization, dA, dB, dC, D ? dD : nullptr,
+                                       delta_bias ? ddelta_bias : nullptr,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("launching complex selective scan backward", e);
+  return MSS_OK;
+}
+
 }  // extern "C"

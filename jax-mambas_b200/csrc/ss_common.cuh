@@ -104,6 +104,41 @@ struct BwdParams {
   float* seg_carry;
 };
 
+// Complex selective scan (ss_cplx.cu): A, B, C, states complex64 (float2),
+// u, delta, z, out, gradients of real arguments fp32; fp32 I/O only.
+struct CplxParams {
+  int batch, dim, seqlen, n_chunks;
+  int delta_softplus;
+  const float* u;
+  const float* delta;
+  const float* z;
+  const void* A;        // (dim, dstate) complex
+  const void* B;        // (batch, dstate, L) complex
+  const void* C;
+  const float* D;
+  const float* delta_bias;
+  const void* h0;       // (batch, dim, dstate) complex or null
+  const int32_t* seq_lens;
+  float* out;
+  float* out_pre;
+  void* last_state;     // complex
+  void* chunk_states;   // (batch, n_chunks, dim, dstate) complex
+  // backward
+  const float* dout;
+  const void* dlast;    // complex
+  float* du;
+  float* ddelta;
+  float* dz;
+  float* dB_acc_r;      // (batch, dstate, L) fp32 planes, zeroed by the launcher
+  float* dB_acc_i;
+  float* dC_acc_r;
+  float* dC_acc_i;
+  float* dA_part;       // (batch, dim, dstate, 2)
+  float* dD_part;       // (batch, dim)
+  float* dbias_part;
+  void* dh0;            // complex
+};
+
 // Causal depthwise conv1d + SiLU (ss_conv.cu); rows are (batch, dim) in the
 // scan's (batch, dim, L) layout.
 struct ConvParams {

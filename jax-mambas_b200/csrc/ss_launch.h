@@ -59,6 +59,18 @@ int conv_segments(int length);
 // state (batch, dim, kwidth - 1), shifted in place.
 cudaError_t launch_conv_step(const ConvParams& p, int kwidth, int io_dtype, cudaStream_t stream);
 
+// Complex scan: forward; backward incl. the batch reductions and the
+// interleaving of dB / dC into complex64 outputs.
+cudaError_t launch_cplx_fwd(const CplxParams& p, int dstate, int zoh, cudaStream_t stream);
+cudaError_t launch_cplx_bwd(const CplxParams& p, int dstate, int zoh, void* dA, void* dB,
+                            void* dC, float* dD, float* ddelta_bias, cudaStream_t stream);
+
+// Fixed-order batch sums of per-batch partials: dA (dim * dstate), dD and
+// ddelta_bias (dim); dD / ddelta_bias may be null.
+cudaError_t launch_param_reduce(const float* dA_part, const float* dD_part,
+                                const float* dbias_part, float* dA, float* dD, float* dbias,
+                                int batch, int dim, int dstate, cudaStream_t stream);
+
 cudaError_t launch_step(const StepParams& p, int dstate, int io_dtype, int zoh,
                         cudaStream_t stream);
 

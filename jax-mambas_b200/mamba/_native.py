@@ -78,6 +78,23 @@ SIGNATURES = {
         ctypes.c_int,
         [_c_void_p, _i32, _i32, _i32, _i32] + [_c_void_p] * 5,  # x weight bias conv_state u
     ),
+    "mamba_ss_complex_chunk_states_elems": (ctypes.c_int64, [_i32, _i32, _i32, _i32]),
+    "mamba_ss_complex_bwd_workspace_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
+    "mamba_ss_complex_fwd": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i32, _i32]
+        + [_c_void_p] * 8  # u delta A B C D z delta_bias
+        + [_i32]  # delta_softplus
+        + [_c_void_p] * 6,  # initial_state seq_lens out out_pre last_state chunk_states
+    ),
+    "mamba_ss_complex_bwd": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i32, _i32]
+        + [_c_void_p] * 8  # u delta A B C D z delta_bias
+        + [_i32]  # delta_softplus
+        + [_c_void_p] * 16  # initial_state seq_lens chunk_states out_pre dout dlast du ddelta dA dB dC dD dz dbias dinit workspace
+        + [ctypes.c_size_t],
+    ),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,

@@ -277,6 +277,124 @@ def fused_step(state, u, delta, A, B, C, D=None, z=None, delta_bias=None,
 
 
 # --------------------------------------------------------------------------
+# Complex SSM (S6 with complex_ssm=True, mamba/mamba1.py:170-176, 196): A, B,
+# C and the state complex, delta and u real; y = Re(C . h) + D u. Gradients of
+# complex arguments are dL/dRe + i dL/dIm (torch's convention; JAX's
+# cotangent is the conjugate).
+# --------------------------------------------------------------------------
+def complex_fused_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                          delta_softplus=False, initial_state=None,
+                          use_euler_barB_approx=True, seq_lens=None):
+    """out (real), last_state (complex) of the complex fused scan."""
+    um, dl, _, _, _, _, D, z, mask = _prepare(
+        u, delta, None, None, None, D, z, delta_bias, delta_softplus, seq_lens, np.float64)
+    A = np.asarray(A, dtype=np.complex128)
+    B = np.asarray(B, dtype=np.complex128)
+    C = np.asarray(C, dtype=np.complex128)
+    batch, dim, L = um.shape
+    N = A.shape[1]
+    h = (np.zeros((batch, dim, N), dtype=np.complex128) if initial_state is None
+         else np.asarray(initial_state, dtype=np.complex128).copy())
+    y = np.empty((batch, dim, L))
+    for t in range(L):
+        dA = dl[:, :, t, None] * A[None]
+        a = np.exp(dA)
+        if use_euler_barB_approx:
+            bbar = dl[:, :, t, None] * B[:, None, :, t]
+        else:
+            bbar = np.expm1(dA) / A[None] * B[:, None, :, t]
+        h = a * h + bbar * um[:, :, t, None]
+        y[:, :, t] = np.einsum("bn,bdn->bd", C[:, :, t], h).real
+    out = y
+    if D is not None:
+        out = out + D[None, :, None] * um
+    if z is not None:
+        out = out * (z * _sigmoid(z))
+    if seq_lens is not None:
+        out = out * mask[:, None, :]
+    return out, h
+
+
+def complex_fused_backward(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                           delta_softplus=False, initial_state=None,
+                           use_euler_barB_approx=True, seq_lens=None, dout=None,
+                           dlast=None):
+    """Analytic adjoint of complex_fused_forward: dict of gradients (complex
+    ones as dL/dRe + i dL/dIm). The adjoint state G = dL/dRe h + i dL/dIm h
+    obeys G_t = dy_t conj(C_t) + conj(a_{t+1}) G_{t+1}."""
+    um, dl, pre, _, _, _, D, z, mask = _prepare(
+        u, delta, None, None, None, D, z, delta_bias, delta_softplus, seq_lens, np.float64)
+    A = np.asarray(A, dtype=np.complex128)
+    B = np.asarray(B, dtype=np.complex128)
+    C = np.asarray(C, dtype=np.complex128)
+    batch, dim, L = um.shape
+    N = A.shape[1]
+    m = mask[:, None, :]
+    dout = np.asarray(dout, dtype=np.float64)
+    h = [None] * (L + 1)
+    h[0] = (np.zeros((batch, dim, N), dtype=np.complex128) if initial_state is None
+            else np.asarray(initial_state, dtype=np.complex128).copy())
+    avals, bvals = [], []
+    for t in range(L):
+        dA = dl[:, :, t, None] * A[None]
+        a = np.exp(dA)
+        bb = (dl[:, :, t, None] + 0j) if use_euler_barB_approx else np.expm1(dA) / A[None]
+        bvals.append(bb)
+        avals.append(a)
+        h[t + 1] = a * h[t] + bb * B[:, None, :, t] * um[:, :, t, None]
+    y = np.stack([np.einsum("bn,bdn->bd", C[:, :, t], h[t + 1]).real for t in range(L)], axis=2)
+    pre_gate = y + (D[None, :, None] * um if D is not None else 0.0)
+    if z is not None:
+        sz = _sigmoid(z)
+        dz = dout * pre_gate * sz * (1.0 + z * (1.0 - sz)) * m
+        dy = dout * z * sz * m
+    else:
+        dz = None
+        dy = dout * m
+    G = (np.zeros((batch, dim, N), dtype=np.complex128) if dlast is None
+         else np.asarray(dlast, dtype=np.complex128).copy())
+    du = np.zeros((batch, dim, L))
+    ddl = np.zeros((batch, dim, L))
+    dA = np.zeros((dim, N), dtype=np.complex128)
+    dB = np.zeros((batch, N, L), dtype=np.complex128)
+    dC = np.zeros((batch, N, L), dtype=np.complex128)
+    for t in range(L - 1, -1, -1):
+        if t + 1 < L:
+            G = np.conj(avals[t + 1]) * G
+        G = G + dy[:, :, t, None] * np.conj(C[:, None, :, t])
+        a, bb, hp = avals[t], bvals[t], h[t]
+        Bt = B[:, None, :, t]
+        ut = um[:, :, t, None]
+        dC[:, :, t] = np.einsum("bd,bdn->bn", dy[:, :, t], np.conj(h[t + 1]))
+        # b_t u_t = bb B u
+        du[:, :, t] = np.sum((G * np.conj(bb * Bt)).real, axis=2)
+        dB[:, :, t] = np.einsum("bdn->bn", G * np.conj(bb) * ut)
+        ga = G * np.conj(hp)  # dL/da
+        Ad = A[None]
+        # a = exp(delta A): da/ddelta = A a, da/dA = delta a
+        ddl[:, :, t] = np.sum((ga * np.conj(Ad * a)).real, axis=2)
+        dA += np.einsum("bdn->dn", ga * np.conj(dl[:, :, t, None] * a))
+        if use_euler_barB_approx:
+            ddl[:, :, t] += np.sum((G * np.conj(Bt * ut)).real, axis=2)
+        else:
+            # bb = expm1(delta A) / A: dbb/ddelta = a, dbb/dA = (delta a - bb) / A
+            gbb = G * np.conj(Bt * ut)
+            ddl[:, :, t] += np.sum((gbb * np.conj(a)).real, axis=2)
+            dA += np.einsum("bdn->dn", gbb * np.conj((dl[:, :, t, None] * a - bb) / Ad))
+    dh0 = np.conj(avals[0]) * G if L > 0 else G
+    du = du + (D[None, :, None] * dy if D is not None else 0.0)
+    du = du * m
+    ddl = ddl * m
+    if delta_softplus:
+        ddl = ddl * _sigmoid(pre)
+    res = {"du": du, "ddelta": ddl, "dA": dA, "dB": dB, "dC": dC,
+           "dD": np.sum(dy * um, axis=(0, 2)) if D is not None else None,
+           "dz": dz, "ddelta_bias": np.sum(ddl, axis=(0, 2)) if delta_bias is not None else None,
+           "dinitial_state": dh0}
+    return res
+
+
+# --------------------------------------------------------------------------
 # Causal depthwise conv1d + SiLU of the Mamba block, (B, D, L) layout.
 # --------------------------------------------------------------------------
 def _conv_prepare(x, weight, bias, seq_lens, conv_state, dtype):
