@@ -536,6 +536,59 @@ def run_conv_bench(args):
         "gpu_launches": args.steps * 3}), flush=True)
 
 
+def run_complex_bench(args):
+    """--config complex: the complex SSM (complex_ssm=True) fused scan forward +
+    backward at the configs[1] shape (B=8, D=1536, L=2048, N=16), fp32 real
+    tensors and complex64 A, B, C. Reported like the real scan (B*D*L
+    elements/s) with the SFU roofline: per state-step the forward evaluates
+    exp and sin/cos of delta A, the backward recomputes them."""
+    import torch
+
+    from mamba.selective_scan_complex import selective_scan_complex_fn
+
+    dev = torch.device("cuda", 0)
+    b, d, L, n = 8, 1536, 2048, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    rnd = lambda *s: torch.randn(*s, generator=g, device=dev)
+    u, dl, z, dout = (rnd(b, d, L) for _ in range(4))
+    A = torch.complex(-0.5 * torch.ones(d, n, device=dev),
+                      torch.arange(n, device=dev, dtype=torch.float32).expand(d, n).contiguous())
+    B = torch.complex(rnd(b, n, L), rnd(b, n, L))
+    C = torch.complex(rnd(b, n, L), rnd(b, n, L))
+    Dp, bias = rnd(d), torch.rand(d, generator=g, device=dev) * 2 - 4
+    leaves = [t.requires_grad_(True) for t in (u, dl, A, B, C, Dp, z, bias)]
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        out = selective_scan_complex_fn(u, dl, A, B, C, Dp, z, bias, True)
+        out.backward(dout)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 20))
+    sampler = ClockSampler(0)
+    with sampler:
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / steps
+    elems = b * d * L
+    print(json.dumps({
+        "metric": "complex selective-scan fwd+bwd B*D*L elements/s", "unit": "Gelem/s",
+        "value": round(elems / (ms * 1e-3) / 1e9, 3), "ms_per_step": round(ms, 4),
+        "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 / complex64", "data": "synthetic", "n_gpus": 1,
+        "config": {"workload": "complex SSM scan at the Mamba-130M layer shape", "batch": b,
+                   "dim": d, "length": L, "dstate": n},
+        "clocks": sampler.summary(), "gpu_launches": steps * 10}), flush=True)
+
+
 # ---------------------------------------------------------------- CPU arm
 def _cpu_sample_shape(cfg, seconds_target):
     # a bounded sample: full length and state size, a slice of the channels
@@ -618,7 +671,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["step", "conv"], default="c1")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["step", "conv", "complex"],
+                    default="c1")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -627,12 +681,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.config in ("step", "conv"):
+    if args.config in ("step", "conv", "complex"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.config} leg has no "
                               "CPU reference arm; see --config c1"}))
         else:
-            (run_step_bench if args.config == "step" else run_conv_bench)(args)
+            {"step": run_step_bench, "conv": run_conv_bench,
+             "complex": run_complex_bench}[args.config](args)
         return
     cfg = CONFIGS[args.config]
     if args.impl == "reference":

@@ -58,10 +58,7 @@ struct TileCfg {
   static constexpr int kCh = 32 / kLPC;       // channels per CTA (one warp)
   // column swizzle of the [channel][state] dB/dC tile: the 32 lanes' float4
   // writes of one state index, and the flush's row reads, avoid bank conflicts
-  static __device__ __forceinline__ int part_swz(int c) {
-    return NS == 16 ? (c & 1) << 2 : NS == 8 ? (c & 3) << 1 : NS == 4 ? (c & 3)
-                                             : NS == 2 ? (c >> 2) & 1 : 0;
-  }
+  static __device__ __forceinline__ int part_swz(int c) { return mss::part_swz<NS>(c); }
 };
 
 struct TileMaps {
@@ -188,42 +185,6 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, 
   }
 }
 
-// Sums one group's [channel][state] tile over the channels and adds state
-// row n's four steps into acc_b[n * L + t] (t = the group's first step).
-// Lane o + NS*h sums channels h*kS .. h*kS + kS - 1 of state o, then the
-// 32/NS lanes of a state combine with xor-shuffles.
-template <int NS>
-__device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_b, int L, int t,
-                                           int len, bool whole, int lane) {
-  using Cfg = TileCfg<NS>;
-  const int o = lane % NS, h = lane / NS;
-  float2 lo = make_float2(0.f, 0.f), hi = lo;
-#pragma unroll
-  for (int i = 0; i < Cfg::kS; ++i) {
-    const int c = h * Cfg::kS + i;
-    const float4 v = part[c][o ^ Cfg::part_swz(c)];
-    lo = add2(lo, make_float2(v.x, v.y));
-    hi = add2(hi, make_float2(v.z, v.w));
-  }
-#pragma unroll
-  for (int m = NS; m < 32; m <<= 1) {
-    lo.x += __shfl_xor_sync(0xffffffffu, lo.x, m);
-    lo.y += __shfl_xor_sync(0xffffffffu, lo.y, m);
-    hi.x += __shfl_xor_sync(0xffffffffu, hi.x, m);
-    hi.y += __shfl_xor_sync(0xffffffffu, hi.y, m);
-  }
-  if (h == 0) {
-    float* gp = acc_b + static_cast<size_t>(o) * L + t;
-    if (whole) {
-      atomicAdd(reinterpret_cast<float4*>(gp), make_float4(lo.x, lo.y, hi.x, hi.y));
-    } else {
-      const float e4[4] = {lo.x, lo.y, hi.x, hi.y};
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (t + e < len) atomicAdd(gp + e, e4[e]);
-    }
-  }
-}
 
 // kSeg: the launch is cut into time segments (blockIdx.z); without it the
 // segment bounds are compile-time constants (one segment of the whole row).

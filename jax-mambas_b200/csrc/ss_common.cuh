@@ -352,4 +352,53 @@ __device__ __forceinline__ float warp_sum32(float v) {
   return v;
 }
 
+// ------------------------------------- channel sums of per-lane (state, step)
+// Backward kernels with the lane layout "kS = min(N, 4) states of one channel
+// per lane, N / kS lanes per channel, one warp per CTA" sum dB / dC over the
+// warp's channels through a [channel][state] shared tile of float4 (4 steps).
+// The column swizzle keeps the 32 lanes' float4 writes of one state slot, and
+// the flush's reads, free of bank conflicts.
+template <int NS>
+__device__ __forceinline__ int part_swz(int c) {
+  return NS == 16 ? (c & 1) << 2 : NS == 8 ? (c & 3) << 1 : NS == 4 ? (c & 3)
+                                           : NS == 2 ? (c >> 2) & 1 : 0;
+}
+
+// Sums one group's [channel][state] tile over the channels and adds state
+// row n's four steps into acc_b[n * L + t] (t = the group's first step).
+// Lane o + NS*h sums channels h*kS .. h*kS + kS - 1 of state o, then the
+// 32/NS lanes of a state combine with xor-shuffles.
+template <int NS>
+__device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_b, int L, int t,
+                                           int len, bool whole, int lane) {
+  constexpr int kS = NS < 4 ? NS : 4;  // states per lane
+  const int o = lane % NS, h = lane / NS;
+  float2 lo = make_float2(0.f, 0.f), hi = lo;
+#pragma unroll
+  for (int i = 0; i < kS; ++i) {
+    const int c = h * kS + i;
+    const float4 v = part[c][o ^ part_swz<NS>(c)];
+    lo = add2(lo, make_float2(v.x, v.y));
+    hi = add2(hi, make_float2(v.z, v.w));
+  }
+#pragma unroll
+  for (int m = NS; m < 32; m <<= 1) {
+    lo.x += __shfl_xor_sync(0xffffffffu, lo.x, m);
+    lo.y += __shfl_xor_sync(0xffffffffu, lo.y, m);
+    hi.x += __shfl_xor_sync(0xffffffffu, hi.x, m);
+    hi.y += __shfl_xor_sync(0xffffffffu, hi.y, m);
+  }
+  if (h == 0) {
+    float* gp = acc_b + static_cast<size_t>(o) * L + t;
+    if (whole) {
+      atomicAdd(reinterpret_cast<float4*>(gp), make_float4(lo.x, lo.y, hi.x, hi.y));
+    } else {
+      const float e4[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (t + e < len) atomicAdd(gp + e, e4[e]);
+    }
+  }
+}
+
 }  // namespace mss

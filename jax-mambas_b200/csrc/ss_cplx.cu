@@ -195,7 +195,11 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
     ss_cbwd_kernel(const CplxParams p) {
   using Cfg = CplxCfg<NS>;
   constexpr int kS = Cfg::kS, kLPC = Cfg::kLPC, kCh = Cfg::kCh, kThreads = Cfg::kThreads;
+  static_assert(Cfg::kWarps == 1, "the channel sums of dB / dC are per warp");
   __shared__ CplxShared sh;
+  // one group's dB (re, im) and dC (re, im) per (channel, swizzled state),
+  // summed over the warp's channels by flush_part
+  __shared__ float4 part[4][kCh][NS];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y, d0 = blockIdx.x * kCh;
   const int L = p.seqlen;
@@ -326,10 +330,13 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
           const Cx dCv = {dy * ht.r, -dy * ht.i};
           const Cx gbb = cmulc(Gt, bbv[e][j]);
           const Cx dBv = {gbb.r * uv, gbb.i * uv};
-          atomicAdd(p.dB_acc_r + (static_cast<size_t>(b) * NS + n) * L + t0 + tg + e, dBv.r);
-          atomicAdd(p.dB_acc_i + (static_cast<size_t>(b) * NS + n) * L + t0 + tg + e, dBv.i);
-          atomicAdd(p.dC_acc_r + (static_cast<size_t>(b) * NS + n) * L + t0 + tg + e, dCv.r);
-          atomicAdd(p.dC_acc_i + (static_cast<size_t>(b) * NS + n) * L + t0 + tg + e, dCv.i);
+          {
+            const int col = n ^ part_swz<NS>(cl);
+            reinterpret_cast<float*>(&part[0][cl][col])[e] = dBv.r;
+            reinterpret_cast<float*>(&part[1][cl][col])[e] = dBv.i;
+            reinterpret_cast<float*>(&part[2][cl][col])[e] = dCv.r;
+            reinterpret_cast<float*>(&part[3][cl][col])[e] = dCv.i;
+          }
           // Euler: Re(G conj(B)) (du = delta * sum, ddelta's b-part u * sum);
           // ZOH: Re(G conj(bb B)) (du = sum). ga = G conj(h_{t-1})
           const Cx gB = kZOH ? cmulc(Gt, cmul(bbv[e][j], Bn)) : cmulc(Gt, Bn);
@@ -355,6 +362,17 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
           Gp[j] = cmulc(Gt, a);  // conj(a_t) G_t, seen by step t - 1
         }
       }
+      // dB, dC of the group: sums over the warp's channels into the planes
+      __syncwarp();
+      {
+        const bool whole = t0 + tg + 4 <= len && (L & 3) == 0;
+        const size_t bo = static_cast<size_t>(b) * NS * L;
+        flush_part<NS>(part[0], p.dB_acc_r + bo, L, t0 + tg, len, whole, lane);
+        flush_part<NS>(part[1], p.dB_acc_i + bo, L, t0 + tg, len, whole, lane);
+        flush_part<NS>(part[2], p.dC_acc_r + bo, L, t0 + tg, len, whole, lane);
+        flush_part<NS>(part[3], p.dC_acc_i + bo, L, t0 + tg, len, whole, lane);
+      }
+      __syncwarp();
       // sums over the channel's lanes, then du, ddelta
 #pragma unroll
       for (int m = 1; m < kLPC; m <<= 1)
