@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       const float* const rdu = &sh.dlu[cl][0];
       float* cs = p.chunk_states + carry_offset(b, t0 / kCkpt, p.n_chunks, p.dim, d, NS) + q * kS;
       const size_t cs_step = static_cast<size_t>(p.dim) * NS;  // next carry index
-#pragma unroll 2
+#pragma unroll 4
       for (int tt = 0; tt < steps; tt += 4) {
         const float4 dl4 = *reinterpret_cast<const float4*>(rdl + tt);
         const float4 du4 = *reinterpret_cast<const float4*>(rdu + tt);
