@@ -589,6 +589,70 @@ def run_complex_bench(args):
         "clocks": sampler.summary(), "gpu_launches": steps * 10}), flush=True)
 
 
+def run_block_bench(args):
+    """--config block: one Mamba block of configs[4]'s 2.8B-shape stack
+    (d_model 2560, d_inner 5120, N 16, dt_rank 160, conv 4, bf16, RMSNorm) on
+    B=8 sequences of L=8192 tokens, forward + backward through
+    mamba.block.MambaBlock (cuBLAS projections in the scan's layout, the conv
+    and scan kernels). --config c3: configs[3]'s 2-layer induction-heads model
+    (d_model 64, B=64, L=256, fp32), forward + backward of the stack.
+    Reported as tokens/s."""
+    import torch
+
+    from mamba.block import MambaBlock, MambaStack
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    if args.config == "block":
+        b, L, dm = 8, 8192, 2560
+        model = MambaBlock(dm, expand=2, d_state=16, norm_type="rmsnorm", num_layers=64,
+                           dtype=torch.bfloat16)
+        x = torch.randn(b, L, dm, generator=g, device=dev, dtype=torch.bfloat16)
+        dout = torch.randn(b, L, dm, generator=g, device=dev, dtype=torch.bfloat16)
+        x.requires_grad_(True)
+
+        def step():
+            model.zero_grad(set_to_none=True)
+            x.grad = None
+            model(x).backward(dout)
+        workload = ("one Mamba block of configs[4]'s 2.8B-shape stack (d_model 2560, "
+                    "d_inner 5120, N 16, dt_rank 160, conv 4, RMSNorm), bf16")
+        dtype = "bf16"
+    else:
+        b, L, vocab = 64, 256, 16
+        model = MambaStack(vocab, 64, 2, expand=2, d_state=16)
+        tokens = torch.randint(1, 15, (b, L), generator=g, device=dev)
+        labels = torch.randint(1, 15, (b,), generator=g, device=dev)
+
+        def step():
+            model.zero_grad(set_to_none=True)
+            loss = torch.nn.functional.cross_entropy(model(tokens)[:, -1], labels)
+            loss.backward()
+        workload = "configs[3]: 2-layer Mamba, d_model 64, induction-heads shape, fp32"
+        dtype = "f32"
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 20))
+    sampler = ClockSampler(0)
+    with sampler:
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / steps
+    print(json.dumps({
+        "metric": "Mamba block fwd+bwd tokens/s", "unit": "tokens/s",
+        "value": round(b * L / (ms * 1e-3), 1), "ms_per_step": round(ms, 3), "steps": steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic", "n_gpus": 1,
+        "config": {"workload": workload, "batch": b, "seq_len": L},
+        "clocks": sampler.summary()}), flush=True)
+
+
 # ---------------------------------------------------------------- CPU arm
 def _cpu_sample_shape(cfg, seconds_target):
     # a bounded sample: full length and state size, a slice of the channels
@@ -671,7 +735,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["step", "conv", "complex"],
+    ap.add_argument("--config",
+                    choices=sorted(CONFIGS) + ["step", "conv", "complex", "block", "c3"],
                     default="c1")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
@@ -681,13 +746,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.config in ("step", "conv", "complex"):
+    if args.config in ("step", "conv", "complex", "block", "c3"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.config} leg has no "
                               "CPU reference arm; see --config c1"}))
         else:
-            {"step": run_step_bench, "conv": run_conv_bench,
-             "complex": run_complex_bench}[args.config](args)
+            {"step": run_step_bench, "conv": run_conv_bench, "complex": run_complex_bench,
+             "block": run_block_bench, "c3": run_block_bench}[args.config](args)
         return
     cfg = CONFIGS[args.config]
     if args.impl == "reference":

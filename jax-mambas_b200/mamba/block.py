@@ -24,6 +24,72 @@ from .causal_conv1d import causal_conv1d_fn
 from .selective_scan_cuda import selective_scan_fn
 
 
+# The projections are batched GEMMs (torch.bmm -> cuBLAS) against weights
+# expanded over the batch with stride 0, so that transposed operands reach
+# cuBLAS as transposed views instead of being copied (torch.matmul folds a
+# 3-D @ 2-D product into one 2-D GEMM and copies a transposed view first).
+def _bw(w, batch):
+    return w.expand(batch, *w.shape)
+
+
+class _ProjIn(torch.autograd.Function):
+    """projed, zpre (B, d_inner, L) = W_main x^T, W_skip x^T for x (B, L, d_model);
+    the backward writes dx in x's layout (the second product accumulates in the
+    GEMM)."""
+
+    @staticmethod
+    def forward(ctx, x, w_main, w_skip):
+        b = x.shape[0]
+        xt = x.transpose(1, 2)
+        ctx.save_for_backward(x, w_main, w_skip)
+        return torch.bmm(_bw(w_main, b), xt), torch.bmm(_bw(w_skip, b), xt)
+
+    @staticmethod
+    def backward(ctx, dp, dz):
+        x, w_main, w_skip = ctx.saved_tensors
+        b = x.shape[0]
+        dx = torch.bmm(dp.transpose(1, 2), _bw(w_main, b))
+        dx = torch.baddbmm(dx, dz.transpose(1, 2), _bw(w_skip, b))
+        return dx, torch.bmm(dp, x).sum(0), torch.bmm(dz, x).sum(0)
+
+
+class _ProjX(torch.autograd.Function):
+    """x_proj of S6 as one GEMM: (dt_r, B, C) = (W_r, W_B, W_C) u for u
+    (B, d_inner, L); B and C come out contiguous (B, N, L), and the backward's
+    du is one GEMM."""
+
+    @staticmethod
+    def forward(ctx, u, w_x, r, n):
+        xp = torch.bmm(_bw(w_x, u.shape[0]), u)
+        ctx.save_for_backward(u, w_x)
+        ctx.rn = (r, n)
+        return xp[:, :r], xp[:, r:r + n].contiguous(), xp[:, r + n:].contiguous()
+
+    @staticmethod
+    def backward(ctx, dr, dB, dC):
+        u, w_x = ctx.saved_tensors
+        dxp = torch.cat([dr, dB, dC], dim=1)
+        du = torch.bmm(_bw(w_x.t(), u.shape[0]), dxp)
+        return du, torch.bmm(dxp, u.transpose(1, 2)).sum(0), None, None
+
+
+class _ProjOut(torch.autograd.Function):
+    """out (B, L, d_model) = y^T W_out^T for y (B, d_inner, L); the backward
+    writes dy in the scan's (B, d_inner, L) layout."""
+
+    @staticmethod
+    def forward(ctx, y, w_out):
+        ctx.save_for_backward(y, w_out)
+        return torch.bmm(y.transpose(1, 2), _bw(w_out.t(), y.shape[0]))
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, w_out = ctx.saved_tensors
+        dt = dout.transpose(1, 2)  # (B, d_model, L) view
+        dy = torch.bmm(_bw(w_out.t(), y.shape[0]), dt)
+        return dy, torch.bmm(dt, y.transpose(1, 2)).sum(0)
+
+
 def _uniform(t, bound, gen):
     with torch.no_grad():
         t.uniform_(-bound, bound, generator=gen)
@@ -90,19 +156,17 @@ class MambaBlock(nn.Module):
         dt = self.act_dtype
         if self.use_norm:
             x = self.norm(x.float()).to(dt)
-        xt = x.to(dt).transpose(1, 2)                       # (B, d_model, L) view
-        projed = torch.matmul(self.w_main.to(dt), xt)       # (B, d_inner, L)
-        zpre = torch.matmul(self.w_skip.to(dt), xt)
+        projed, zpre = _ProjIn.apply(x.to(dt), self.w_main.to(dt),
+                                     self.w_skip.to(dt))   # (B, d_inner, L)
         # mask * silu(conv(mask * projed)) (the conv masks by seq_lens)
         u = causal_conv1d_fn(projed, self.conv_w, self.conv_b, seq_lens)
-        dtr = torch.matmul(self.w_r.to(dt), u)              # (B, dt_rank, L)
-        Bm = torch.matmul(self.w_B.to(dt), u)                # (B, N, L)
-        Cm = torch.matmul(self.w_C.to(dt), u)
-        delta = torch.matmul(self.w_dt.to(dt), dtr)          # (B, d_inner, L), bias in the scan
+        w_x = torch.cat([self.w_r, self.w_B, self.w_C], dim=0).to(dt)
+        dtr, Bm, Cm = _ProjX.apply(u, w_x, self.dt_rank, self.d_state)  # (B, r / N / N, L)
+        delta = torch.bmm(_bw(self.w_dt.to(dt), u.shape[0]), dtr)  # (B, d_inner, L); bias in the scan
         A = -torch.exp(self.A_log)
         y = selective_scan_fn(u, delta, A, Bm, Cm, self.D, zpre, self.dt_bias, True,
                               seq_lens=seq_lens)             # (scan + D u) * silu(skip)
-        out = torch.matmul(y.transpose(1, 2), self.w_out.to(dt).t())  # (B, L, d_model)
+        out = _ProjOut.apply(y, self.w_out.to(dt))         # (B, L, d_model)
         return res + out.to(res.dtype)
 
 
