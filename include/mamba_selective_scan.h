@@ -119,6 +119,9 @@ mss_status mamba_ss_bwd(void* stream, int32_t discretization, int32_t batch,
  * and input gradients are written as exact zeros.
  * io_dtype (MSS_F32 or MSS_BF16) types u, delta, z, B, C, out and their
  * gradients; the state, A, D, delta_bias and reductions stay fp32.
+ * chunk_states (the saved carries the backward reads) may be NULL in the
+ * forward when no backward follows; the scan then also runs without time
+ * segments.
  * ------------------------------------------------------------------------- */
 mss_status mamba_ss_fused_fwd(
     void* stream, int32_t io_dtype, int32_t discretization, int32_t batch,

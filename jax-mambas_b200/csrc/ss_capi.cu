@@ -163,10 +163,9 @@ mss_status mamba_ss_fused_fwd(
   mss_status st = check_dims("mamba_ss_fused_fwd", io_dtype, discretization,
                              batch, length, dim, dstate);
   if (st != MSS_OK) return st;
-  if (!u || !delta || !A || !B || !C || !out || !chunk_states)
+  if (!u || !delta || !A || !B || !C || !out)
     return fail(MSS_INVALID_ARGUMENT,
-                "mamba_ss_fused_fwd: u, delta, A, B, C, out and chunk_states "
-                "must be non-null");
+                "mamba_ss_fused_fwd: u, delta, A, B, C and out must be non-null");
   if (reinterpret_cast<uintptr_t>(chunk_states) & 15)
     return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_fwd: chunk_states must be 16-byte aligned");
   mss::FwdParams p{};

@@ -312,6 +312,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
                     "rawC follows rawB");
       const float* const rdl = &sh.dlt[cl][0];
       const float* const rdu = &sh.dlu[cl][0];
+      const bool save_carries = p.chunk_states != nullptr;
       float* cs = p.chunk_states + carry_offset(b, t0 / kCkpt, p.n_chunks, p.dim, d, NS) + q * kS;
       const size_t cs_step = static_cast<size_t>(p.dim) * NS;  // next carry index
 #pragma unroll 4
@@ -386,8 +387,8 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
             for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] += yp[e];
           }
           // carry after these 4 steps (entries past the valid length are not
-          // written: the backward never reads them)
-          if (lane_active) {
+          // written: the backward never reads them; none for forward-only calls)
+          if (lane_active && save_carries) {
             if constexpr (kS == 4) {
               *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
             } else {
@@ -574,7 +575,10 @@ cudaError_t launch_fwd(const FwdParams& p_in, int dstate, int io_dtype, int zoh,
   FwdParams p = p_in;
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
   // time segments; their scratch follows the carries in chunk_states
-  const SegPlan sp = seg_plan(p.batch, p.seqlen, p.dim, dstate);
+  // (a forward-only call without chunk_states runs unsegmented: the segment
+  // scratch lives in chunk_states)
+  const SegPlan sp = p.chunk_states ? seg_plan(p.batch, p.seqlen, p.dim, dstate)
+                                    : SegPlan{1, (p.seqlen + kTile - 1) / kTile};
   p.n_seg = sp.n_seg;
   p.seg_tiles = sp.seg_tiles;
   if (p.n_seg > 1) {

@@ -245,10 +245,14 @@ class _FusedScan(torch.autograd.Function):
         batch, dim, length = u.shape
         n = A.shape[1]
         out = torch.empty_like(u)
-        pre = torch.empty_like(u) if z is not None else None
+        # saved carries and the pre-gate output only when a backward can follow
+        # (needs_input_grad is all False under no_grad; grad mode itself is
+        # always off inside forward)
+        grads = any(ctx.needs_input_grad[:9])
+        pre = torch.empty_like(u) if (z is not None and grads) else None
         last = torch.empty((batch, dim, n), dtype=torch.float32, device=u.device)
-        cs = torch.empty(chunk_states_elems(batch, length, dim, n),
-                         dtype=torch.float32, device=u.device)
+        cs = (torch.empty(chunk_states_elems(batch, length, dim, n),
+                          dtype=torch.float32, device=u.device) if grads else None)
         fused_forward_into(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
                            initial_state, seq_lens, out, last, cs, zoh, pre)
         ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, initial_state,

@@ -230,3 +230,23 @@ def test_invalid_arguments_raise_without_launch():
                                torch.zeros(1, 3, 8, device="cuda"),
                                torch.zeros(1, 3, 8, device="cuda"), None, None, None,
                                False, None, None, u, None, torch.zeros(64, device="cuda"))
+
+
+def test_forward_only_skips_the_saved_state():
+    """Under torch.no_grad the forward writes no carries and no pre-gate
+    output (chunk_states = NULL); the outputs equal the oracle's and those of
+    a grad-enabled run on the same inputs."""
+    from mamba.selective_scan_cuda import selective_scan_fn
+
+    x = orc.make_inputs(2, 16, 700, 16, seed=31, initial_state=True)
+    ref = oracle_fused(x)
+    with torch.no_grad():
+        res = run_fused(x, grads=False)
+    _check(res, ref, keys=())
+    t = {k: to_dev(x[k]) for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias",
+                                   "initial_state")}
+    t["u"].requires_grad_(True)
+    out, last = selective_scan_fn(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
+                                  t["delta_bias"], True, True, initial_state=t["initial_state"])
+    assert_close(res["out"], out.detach().cpu().numpy(), FWD_TOL, "out")
+    assert_close(res["last_state"], last.detach().cpu().numpy(), FWD_TOL, "last_state")
