@@ -30,6 +30,7 @@
 
 #include <cstddef>
 #include <cstring>
+#include <type_traits>
 
 #include "ss_common.cuh"
 #include "ss_launch.h"
@@ -195,6 +196,21 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
     if (!kEnd) tma_load_2d(&sh.rawC[s][0][0], &maps.c, t0, b * NS, bar);
   };
 
+  // transform / emit items (4 steps of one channel): lane tid takes steps
+  // (tid % 8) * 4 .. + 3 of channels tid / 8 + k * kItemChStride
+  constexpr int kItems = kCh * (kTile / 4) / kThreads;
+  constexpr int kItemChStride = kThreads / (kTile / 4);
+  static_assert(kItems * kItemChStride == kCh, "items cover the channels");
+  const int it_tt = (tid % (kTile / 4)) * 4;
+  const int it_c0 = tid / (kTile / 4);
+  float it_bias[kItems], it_D[kItems];
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    const int c = it_c0 + k * kItemChStride;
+    it_bias[k] = (p.delta_bias && c < n_ch) ? __ldg(p.delta_bias + d0 + c) : 0.f;
+    it_D[k] = (p.D && c < n_ch) ? __ldg(p.D + d0 + c) : 0.f;
+  }
+
   if (use_tma) {
     if (tid == 0) {
       mbar_init(&sh.bar[0], 1);
@@ -226,41 +242,54 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       }
     }
 
+    // whole tile: every channel live, every step valid, staged by TMA; the
+    // transform and emit then run without per-element predicates
+    const bool full = use_tma && n_ch == kCh && t0 + kTile <= len;
     if (t0 < len) {
       // ---- 1. transform the tile into fp32 work tiles, 4 steps per item
-      for (int i = tid; i < kCh * (kTile / 4); i += kThreads) {
-        const int c = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
-        float x[4] = {0.f, 0.f, 0.f, 0.f}, uv[4] = {0.f, 0.f, 0.f, 0.f};
-        if (c < n_ch) {
-          if (use_tma) {
+      auto transform = [&](auto full_t) {
+        constexpr bool kFull = decltype(full_t)::value;
+#pragma unroll
+        for (int k = 0; k < kItems; ++k) {
+          const int c = it_c0 + k * kItemChStride, tt = it_tt;
+          float x[4] = {0.f, 0.f, 0.f, 0.f}, uv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (kFull) {
             load4_smem(&sh.rawD[s][c][tt], x);
             load4_smem(&sh.rawU[s][c][tt], uv);
-          } else {
-            const size_t off = static_cast<size_t>(d0 + c) * L + t0 + tt;
+          } else if (c < n_ch) {
+            if (use_tma) {
+              load4_smem(&sh.rawD[s][c][tt], x);
+              load4_smem(&sh.rawU[s][c][tt], uv);
+            } else {
+              const size_t off = static_cast<size_t>(d0 + c) * L + t0 + tt;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (t0 + tt + e < len) {
-                x[e] = Elem<T>::ld(dl_b + off + e);
-                uv[e] = Elem<T>::ld(u_b + off + e);
+              for (int e = 0; e < 4; ++e) {
+                if (t0 + tt + e < len) {
+                  x[e] = Elem<T>::ld(dl_b + off + e);
+                  uv[e] = Elem<T>::ld(u_b + off + e);
+                }
               }
             }
           }
-        }
-        const float bias = (p.delta_bias && c < n_ch) ? __ldg(p.delta_bias + d0 + c) : 0.f;
-        const float Dd = (p.D && c < n_ch) ? __ldg(p.D + d0 + c) : 0.f;
-        float dv[4], du[4], yd[4];
+          float dv[4], du[4], yd[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const bool valid = c < n_ch && t0 + tt + e < len;
-          const float xe = x[e] + bias;
-          const float de = p.delta_softplus ? softplus_f(xe) : xe;
-          dv[e] = valid ? de : 0.f;
-          du[e] = valid ? (kZOH ? uv[e] : de * uv[e]) : 0.f;
-          yd[e] = valid ? Dd * uv[e] : 0.f;
+          for (int e = 0; e < 4; ++e) {
+            const bool valid = kFull || (c < n_ch && t0 + tt + e < len);
+            const float xe = x[e] + it_bias[k];
+            const float de = p.delta_softplus ? softplus_f(xe) : xe;
+            dv[e] = valid ? de : 0.f;
+            du[e] = valid ? (kZOH ? uv[e] : de * uv[e]) : 0.f;
+            yd[e] = valid ? it_D[k] * uv[e] : 0.f;
+          }
+          *reinterpret_cast<float4*>(&sh.dlt[c][tt]) = make_float4(dv[0], dv[1], dv[2], dv[3]);
+          *reinterpret_cast<float4*>(&sh.dlu[c][tt]) = make_float4(du[0], du[1], du[2], du[3]);
+          *reinterpret_cast<float4*>(&sh.ys[c][tt]) = make_float4(yd[0], yd[1], yd[2], yd[3]);
         }
-        *reinterpret_cast<float4*>(&sh.dlt[c][tt]) = make_float4(dv[0], dv[1], dv[2], dv[3]);
-        *reinterpret_cast<float4*>(&sh.dlu[c][tt]) = make_float4(du[0], du[1], du[2], du[3]);
-        *reinterpret_cast<float4*>(&sh.ys[c][tt]) = make_float4(yd[0], yd[1], yd[2], yd[3]);
+      };
+      if (full) {
+        transform(std::true_type{});
+      } else {
+        transform(std::false_type{});
       }
       if (!(kDirectBC && use_tma)) {
         for (int i = tid; i < NS * (kTile / 4); i += kThreads) {
@@ -405,42 +434,54 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
 
     if constexpr (!kEnd) {
       // ---- 3. emit out = (y + D u) * silu(z), and y + D u, 4 steps per item
-      for (int i = tid; i < kCh * (kTile / 4); i += kThreads) {
-        const int c = i / (kTile / 4), tt = (i % (kTile / 4)) * 4;
-        const int t = t0 + tt;
-        if (c >= n_ch || t >= L) continue;
-        const size_t off = static_cast<size_t>(d0 + c) * L + t;
-        float o[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f};
-        if (t < len) {
-          float zv[4];
-          if (z_b) {
-            if (use_tma) {
-              load4_smem(&sh.rawZ[s][c][tt], zv);
-            } else {
+      auto emit = [&](auto full_t) {
+        constexpr bool kFull = decltype(full_t)::value;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+        for (int k = 0; k < kItems; ++k) {
+          const int c = it_c0 + k * kItemChStride, tt = it_tt;
+          const int t = t0 + tt;
+          if (!kFull && (c >= n_ch || t >= L)) continue;
+          const size_t off = static_cast<size_t>(d0 + c) * L + t;
+          float o[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f};
+          if (kFull || t < len) {
+            float zv[4];
+            if (z_b) {
+              if (kFull || use_tma) {
+                load4_smem(&sh.rawZ[s][c][tt], zv);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+              }
+            }
+            const float4 y4 = *reinterpret_cast<const float4*>(&sh.ys[c][tt]);
+            const float ys4[4] = {y4.x, y4.y, y4.z, y4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (kFull || t + e < len) {
+                pre[e] = ys4[e];
+                o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
+              }
             }
           }
+          if (kFull || use_tma) {  // whole, aligned groups: L is a multiple of 4 here
+            store4_global(out_b + off, o);
+            if (pre_b) store4_global(pre_b + off, pre);
+          } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (t + e < len) {
-              pre[e] = sh.ys[c][tt + e];
-              o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
+            for (int e = 0; e < 4; ++e) {
+              if (t + e < L) {
+                Elem<T>::st(out_b + off + e, o[e]);
+                if (pre_b) Elem<T>::st(pre_b + off + e, pre[e]);
+              }
             }
           }
         }
-        if (use_tma) {  // whole, aligned groups: L is a multiple of 4 here
-          store4_global(out_b + off, o);
-          if (pre_b) store4_global(pre_b + off, pre);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (t + e < L) {
-              Elem<T>::st(out_b + off + e, o[e]);
-              if (pre_b) Elem<T>::st(pre_b + off + e, pre[e]);
-            }
-          }
-        }
+      };
+      if (full) {
+        emit(std::true_type{});
+      } else {
+        emit(std::false_type{});
       }
     }
     __syncthreads();
