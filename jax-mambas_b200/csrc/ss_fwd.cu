@@ -16,7 +16,7 @@
 //      staging buffer, completing on an mbarrier; the TMA zero-fills past the
 //      sequence end and past the last channel; the next tile's copies fly
 //      while this tile computes;
-//   1. transform: delta_eff = softplus(delta + bias), delta_eff*u and D*u are
+//   1. transform: delta_eff = softplus(delta + bias) and delta_eff*u are
 //      formed once per element into fp32 work tiles, B and C are widened;
 //   2. scan: each lane steps through the tile; per step and state one
 //      2^(delta*A*log2 e) on the SFU and packed fp32x2 multiply-adds, then the
@@ -75,7 +75,7 @@ struct FwdShared {
   // fp32 work tiles
   float dlt[kCh][kRow];  // delta_eff
   float dlu[kCh][kRow];  // delta_eff * u   (ZOH: u)
-  float ys[kCh][kRow];   // D u, then + sum_n C_t h_t
+  float ys[kCh][kRow];   // sum_n C_t h_t
   // widened B/C (bf16 I/O only; fp32 I/O reads the swizzled staging)
   float Bs[sizeof(T) == 4 ? 1 : NS][kRow];
   float Cs[sizeof(T) == 4 ? 1 : NS][kRow];
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
               }
             }
           }
-          float dv[4], du[4], yd[4];
+          float dv[4], du[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const bool valid = kFull || (c < n_ch && t0 + tt + e < len);
@@ -279,11 +279,9 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
             const float de = p.delta_softplus ? softplus_f(xe) : xe;
             dv[e] = valid ? de : 0.f;
             du[e] = valid ? (kZOH ? uv[e] : de * uv[e]) : 0.f;
-            yd[e] = valid ? it_D[k] * uv[e] : 0.f;
           }
           *reinterpret_cast<float4*>(&sh.dlt[c][tt]) = make_float4(dv[0], dv[1], dv[2], dv[3]);
           *reinterpret_cast<float4*>(&sh.dlu[c][tt]) = make_float4(du[0], du[1], du[2], du[3]);
-          *reinterpret_cast<float4*>(&sh.ys[c][tt]) = make_float4(yd[0], yd[1], yd[2], yd[3]);
         }
       };
       if (full) {
@@ -327,13 +325,15 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       // kLPC lanes of a channel read adjacent B/C rows (distinct banks) and
       // pairs of steps are packed into fp32x2 operations.
       const int steps = min(kTile, len - t0);
-      // this lane's rows (pointers and swizzle keys, fixed over the tile)
-      const float* rB[kS];
-      int kB[kS];
+      // this lane's B rows as byte offsets into shared memory with the
+      // swizzle key folded in: rows are 128-byte aligned, so the 16-byte
+      // chunk of group g sits at oB[j] ^ (g << 4)
+      const char* const smem_c = reinterpret_cast<const char*>(smem_raw);
+      uint32_t oB[kS];
 #pragma unroll
       for (int j = 0; j < kS; ++j) {
-        rB[j] = reinterpret_cast<const float*>(&sh.rawB[s][st_of(j)][0]);
-        kB[j] = st_of(j) & 7;
+        const char* row_b = reinterpret_cast<const char*>(&sh.rawB[s][st_of(j)][0]);
+        oB[j] = static_cast<uint32_t>(row_b - smem_c) | ((st_of(j) & 7) << 4);
       }
       using Sh = FwdShared<NS, T>;
       constexpr int kCfromB = 2 * Sh::kNSP * kTile;  // rawC - rawB, elements
@@ -344,89 +344,98 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
       const bool save_carries = p.chunk_states != nullptr;
       float* cs = p.chunk_states + carry_offset(b, t0 / kCkpt, p.n_chunks, p.dim, d, NS) + q * kS;
       const size_t cs_step = static_cast<size_t>(p.dim) * NS;  // next carry index
+      auto scan = [&](auto full_t) {
+        constexpr bool kFull = decltype(full_t)::value;
+        const int n_steps = kFull ? kTile : steps;
 #pragma unroll 4
-      for (int tt = 0; tt < steps; tt += 4) {
-        const float4 dl4 = *reinterpret_cast<const float4*>(rdl + tt);
-        const float4 du4 = *reinterpret_cast<const float4*>(rdu + tt);
-        const float2 dlp[2] = {make_float2(dl4.x, dl4.y), make_float2(dl4.z, dl4.w)};
-        const float2 dup_[2] = {make_float2(du4.x, du4.y), make_float2(du4.z, du4.w)};
-        float2 yp2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        for (int tt = 0; tt < n_steps; tt += 4) {
+          const float4 dl4 = *reinterpret_cast<const float4*>(rdl + tt);
+          const float4 du4 = *reinterpret_cast<const float4*>(rdu + tt);
+          const float2 dlp[2] = {make_float2(dl4.x, dl4.y), make_float2(dl4.z, dl4.w)};
+          const float2 dup_[2] = {make_float2(du4.x, du4.y), make_float2(du4.z, du4.w)};
+          float2 yp2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int j = 0; j < kS; ++j) {
-          const int n = st_of(j);
-          float4 B4, C4;
-          if constexpr (kDirectBC) {
-            // 16-byte chunk tt/4 of row n sits at chunk (tt/4) ^ (n & 7)
-            const int col = ((tt >> 2) ^ kB[j]) << 2;
-            B4 = *reinterpret_cast<const float4*>(rB[j] + col);
-            C4 = *reinterpret_cast<const float4*>(rB[j] + kCfromB + col);
-          } else {
-            B4 = *reinterpret_cast<const float4*>(&sh.Bs[n][tt]);
-            C4 = *reinterpret_cast<const float4*>(&sh.Cs[n][tt]);
-          }
-          const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
-          const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
-          const float2 a2p = dup2(a2[j]);
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float2 arg = mul2(dlp[e], a2p);
-            const float2 ab = make_float2(ex2(arg.x), ex2(arg.y));
-            float2 bu;
-            if constexpr (kZOH) {
-              // b_bar = expm1(delta*A) / A * B   (mamba/selective_scan_cuda.py:77)
-              const float inv = 1.f / Av[j];
-              bu.x = Bp[e].x * (expm1f(dlp[e].x * Av[j]) * inv) * dup_[e].x;
-              bu.y = Bp[e].y * (expm1f(dlp[e].y * Av[j]) * inv) * dup_[e].y;
+          for (int j = 0; j < kS; ++j) {
+            const int n = st_of(j);
+            float4 B4, C4;
+            if constexpr (kDirectBC) {
+              // 16-byte chunk tt/4 of row n sits at chunk (tt/4) ^ (n & 7)
+              const char* pb = smem_c + (oB[j] ^ static_cast<uint32_t>(tt << 2));
+              B4 = *reinterpret_cast<const float4*>(pb);
+              C4 = *reinterpret_cast<const float4*>(pb + kCfromB * sizeof(float));
             } else {
-              bu = mul2(Bp[e], dup_[e]);
+              B4 = *reinterpret_cast<const float4*>(&sh.Bs[n][tt]);
+              C4 = *reinterpret_cast<const float4*>(&sh.Cs[n][tt]);
             }
-            float2 hh;
-            hh.x = h[j] = fmaf(ab.x, h[j], bu.x);
-            hh.y = h[j] = fmaf(ab.y, h[j], bu.y);
-            yp2[e] = fma2(Cp[e], hh, yp2[e]);
-          }
-        }
-        if constexpr (kEnd) {
-          dsum += (dl4.x + dl4.y) + (dl4.z + dl4.w);
-        } else {
-          const float yp[4] = {yp2[0].x, yp2[0].y, yp2[1].x, yp2[1].y};
-          // sum the kLPC lanes of a channel (reduce-scatter: lane q keeps the
-          // steps it will store)
-          if constexpr (kLPC == 4) {
-            const bool hi2 = (q & 2) != 0;
-            const float s0 = hi2 ? yp[0] : yp[2], s1 = hi2 ? yp[1] : yp[3];
-            float k0 = hi2 ? yp[2] : yp[0], k1 = hi2 ? yp[3] : yp[1];
-            k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-            k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-            const bool hi1 = (q & 1) != 0;
-            const float sx = hi1 ? k0 : k1;
-            float kk = hi1 ? k1 : k0;
-            kk += __shfl_xor_sync(0xffffffffu, sx, 1);
-            sh.ys[cl][tt + q] += kk;  // step tt + q
-          } else if constexpr (kLPC == 2) {
-            const bool hi = (q & 1) != 0;
-            const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
-            float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
-            k0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-            k1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-            sh.ys[cl][tt + 2 * q] += k0;
-            sh.ys[cl][tt + 2 * q + 1] += k1;
-          } else {
+            const float2 Bp[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
+            const float2 Cp[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
+            const float2 a2p = dup2(a2[j]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] += yp[e];
-          }
-          // carry after these 4 steps (entries past the valid length are not
-          // written: the backward never reads them; none for forward-only calls)
-          if (lane_active && save_carries) {
-            if constexpr (kS == 4) {
-              *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < kS; ++j) cs[j] = h[j];
+            for (int e = 0; e < 2; ++e) {
+              const float2 arg = mul2(dlp[e], a2p);
+              const float2 ab = make_float2(ex2(arg.x), ex2(arg.y));
+              float2 bu;
+              if constexpr (kZOH) {
+                // b_bar = expm1(delta*A) / A * B   (mamba/selective_scan_cuda.py:77)
+                const float inv = 1.f / Av[j];
+                bu.x = Bp[e].x * (expm1f(dlp[e].x * Av[j]) * inv) * dup_[e].x;
+                bu.y = Bp[e].y * (expm1f(dlp[e].y * Av[j]) * inv) * dup_[e].y;
+              } else {
+                bu = mul2(Bp[e], dup_[e]);
+              }
+              float2 hh;
+              hh.x = h[j] = fmaf(ab.x, h[j], bu.x);
+              hh.y = h[j] = fmaf(ab.y, h[j], bu.y);
+              yp2[e] = fma2(Cp[e], hh, yp2[e]);
             }
           }
-          cs += cs_step;
+          if constexpr (kEnd) {
+            dsum += (dl4.x + dl4.y) + (dl4.z + dl4.w);
+          } else {
+            const float yp[4] = {yp2[0].x, yp2[0].y, yp2[1].x, yp2[1].y};
+            // sum the kLPC lanes of a channel (reduce-scatter: lane q keeps the
+            // steps it will store)
+            if constexpr (kLPC == 4) {
+              const bool hi2 = (q & 2) != 0;
+              const float s0 = hi2 ? yp[0] : yp[2], s1 = hi2 ? yp[1] : yp[3];
+              float k0 = hi2 ? yp[2] : yp[0], k1 = hi2 ? yp[3] : yp[1];
+              k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+              k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+              const bool hi1 = (q & 1) != 0;
+              const float sx = hi1 ? k0 : k1;
+              float kk = hi1 ? k1 : k0;
+              kk += __shfl_xor_sync(0xffffffffu, sx, 1);
+              sh.ys[cl][tt + q] = kk;  // step tt + q
+            } else if constexpr (kLPC == 2) {
+              const bool hi = (q & 1) != 0;
+              const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
+              float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
+              k0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+              k1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+              sh.ys[cl][tt + 2 * q] = k0;
+              sh.ys[cl][tt + 2 * q + 1] = k1;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] = yp[e];
+            }
+            // carry after these 4 steps (entries past the valid length are not
+            // written: the backward never reads them; none for forward-only calls)
+            if (lane_active && save_carries) {
+              if constexpr (kS == 4) {
+                *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < kS; ++j) cs[j] = h[j];
+              }
+            }
+            cs += cs_step;
+          }
         }
+      };
+      if (full) {
+        scan(std::true_type{});
+      } else {
+        scan(std::false_type{});
       }
     }
 
@@ -444,14 +453,17 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
           const size_t off = static_cast<size_t>(d0 + c) * L + t;
           float o[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f};
           if (kFull || t < len) {
-            float zv[4];
-            if (z_b) {
-              if (kFull || use_tma) {
-                load4_smem(&sh.rawZ[s][c][tt], zv);
-              } else {
+            // the raw u and z of this tile are still staged (the buffer is
+            // refilled only after the tile's closing barrier)
+            float zv[4], uv[4];
+            if (kFull || use_tma) {
+              load4_smem(&sh.rawU[s][c][tt], uv);
+              if (z_b) load4_smem(&sh.rawZ[s][c][tt], zv);
+            } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+              for (int e = 0; e < 4; ++e) {
+                uv[e] = t + e < len ? Elem<T>::ld(u_b + off + e) : 0.f;
+                if (z_b) zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
               }
             }
             const float4 y4 = *reinterpret_cast<const float4*>(&sh.ys[c][tt]);
@@ -459,7 +471,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (kFull || t + e < len) {
-                pre[e] = ys4[e];
+                pre[e] = fmaf(it_D[k], uv[e], ys4[e]);
                 o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
               }
             }
