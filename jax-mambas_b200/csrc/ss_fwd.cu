@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstddef>
+#include <cstdlib>
 #include <cstring>
 #include <type_traits>
 
@@ -44,12 +45,15 @@ constexpr int kPad = 4;    // row padding (floats) of the fp32 work tiles
 constexpr int kRow = kTile + kPad;
 static_assert(kTile % kCkpt == 0 && kCkpt == 4, "a carry is saved after every 4 steps");
 
-template <int NS>
+// kWide: four warps per CTA share one B/C staging (N = 16 only; chosen for
+// grids of several waves, where the smaller shared-memory share per warp
+// lets more warps reside per SM)
+template <int NS, bool kWide = false>
 struct FwdCfg {
   static constexpr int kS = NS < 4 ? NS : 4;  // states per lane
   static constexpr int kLPC = NS / kS;        // lanes per channel
   static constexpr int kCPW = 32 / kLPC;      // channels per warp
-  static constexpr int kCh = kCPW < 8 ? 8 : kCPW;  // channels per CTA
+  static constexpr int kCh = kWide ? 4 * kCPW : (kCPW < 8 ? 8 : kCPW);  // channels per CTA
   static constexpr int kWarps = kCh / kCPW;   // warps per CTA
   static constexpr int kThreads = kWarps * 32;
 };
@@ -59,9 +63,9 @@ struct FwdMaps {
   CUtensorMap d, u, z, b, c;
 };
 
-template <int NS, typename T>
+template <int NS, typename T, bool kWide = false>
 struct FwdShared {
-  static constexpr int kCh = FwdCfg<NS>::kCh;
+  static constexpr int kCh = FwdCfg<NS, kWide>::kCh;
   // staging, written by TMA (two buffers); every block is a multiple of 128 B
   alignas(128) T rawD[2][kCh][kTile];
   T rawU[2][kCh][kTile];
@@ -105,10 +109,10 @@ __device__ __forceinline__ void store4_global(__nv_bfloat16* dst, const float (&
 
 // kEnd: the end-state pass of a segmented scan (no outputs; each segment from
 // a zero state, its final state and sum of delta_eff to seg_end / seg_dsum).
-template <int NS, typename T, bool kZOH, bool kEnd>
-__global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
+template <int NS, typename T, bool kZOH, bool kEnd, bool kWide>
+__global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     ss_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
-  using Cfg = FwdCfg<NS>;
+  using Cfg = FwdCfg<NS, kWide>;
   constexpr int kS = Cfg::kS;
   constexpr int kLPC = Cfg::kLPC;
   constexpr int kCh = Cfg::kCh;
@@ -118,7 +122,8 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
   // delta = 0, so they never touch the state.
   constexpr bool kDirectBC = sizeof(T) == 4;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  FwdShared<NS, T>& sh = *reinterpret_cast<FwdShared<NS, T>*>(smem_raw);
+  using Sh = FwdShared<NS, T, kWide>;
+  Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -335,7 +340,6 @@ __global__ void __launch_bounds__(FwdCfg<NS>::kThreads)
         const char* row_b = reinterpret_cast<const char*>(&sh.rawB[s][st_of(j)][0]);
         oB[j] = static_cast<uint32_t>(row_b - smem_c) | ((st_of(j) & 7) << 4);
       }
-      using Sh = FwdShared<NS, T>;
       constexpr int kCfromB = 2 * Sh::kNSP * kTile;  // rawC - rawB, elements
       static_assert(offsetof(Sh, rawC) - offsetof(Sh, rawB) == kCfromB * sizeof(T),
                     "rawC follows rawB");
@@ -539,12 +543,25 @@ __global__ void seg_combine_fwd_kernel(const float* __restrict__ A, const float*
 }
 
 template <int NS, typename T, bool kZOH>
-static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps,
+static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps, bool wide,
                                 cudaStream_t stream) {
+  if constexpr (NS == 16) {
+    if (wide) {  // unsegmented only
+      using CfgW = FwdCfg<NS, true>;
+      const size_t smem_w = sizeof(FwdShared<NS, T, true>);
+      auto kern_w = ss_fwd_kernel<NS, T, kZOH, false, true>;
+      cudaError_t e = cudaFuncSetAttribute(
+          kern_w, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_w));
+      if (e != cudaSuccess) return e;
+      const unsigned gxw = (p.dim + CfgW::kCh - 1) / CfgW::kCh;
+      kern_w<<<dim3(gxw, p.batch, 1), CfgW::kThreads, smem_w, stream>>>(p, maps);
+      return cudaPeekAtLastError();
+    }
+  }
   using Cfg = FwdCfg<NS>;
   const size_t smem = sizeof(FwdShared<NS, T>);
-  auto kern = ss_fwd_kernel<NS, T, kZOH, false>;
-  auto kern_end = ss_fwd_kernel<NS, T, kZOH, true>;
+  auto kern = ss_fwd_kernel<NS, T, kZOH, false, false>;
+  auto kern_end = ss_fwd_kernel<NS, T, kZOH, true, false>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -564,14 +581,14 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps,
 }
 
 template <typename T, bool kZOH>
-static cudaError_t launch_fwd_n(const FwdParams& p, const FwdMaps& maps, int dstate,
+static cudaError_t launch_fwd_n(const FwdParams& p, const FwdMaps& maps, int dstate, bool wide,
                                 cudaStream_t stream) {
   switch (dstate) {
-    case 1: return launch_fwd_t<1, T, kZOH>(p, maps, stream);
-    case 2: return launch_fwd_t<2, T, kZOH>(p, maps, stream);
-    case 4: return launch_fwd_t<4, T, kZOH>(p, maps, stream);
-    case 8: return launch_fwd_t<8, T, kZOH>(p, maps, stream);
-    case 16: return launch_fwd_t<16, T, kZOH>(p, maps, stream);
+    case 1: return launch_fwd_t<1, T, kZOH>(p, maps, false, stream);
+    case 2: return launch_fwd_t<2, T, kZOH>(p, maps, false, stream);
+    case 4: return launch_fwd_t<4, T, kZOH>(p, maps, false, stream);
+    case 8: return launch_fwd_t<8, T, kZOH>(p, maps, false, stream);
+    case 16: return launch_fwd_t<16, T, kZOH>(p, maps, wide, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -641,6 +658,13 @@ cudaError_t launch_fwd(const FwdParams& p_in, int dstate, int io_dtype, int zoh,
     p.seg_in = scratch + bds * dstate;
     p.seg_dsum = scratch + 2 * bds * dstate;
   }
+  // four-warp CTAs (N = 16) once the one-warp grid fills the GPU (8 or more
+  // CTAs per SM); smaller grids keep the finer one-warp work units
+  const long long narrow_ctas =
+      static_cast<long long>(p.batch) * ((p.dim + FwdCfg<16>::kCh - 1) / FwdCfg<16>::kCh);
+  bool wide = narrow_ctas >= 148LL * 8;
+  if (const char* env = getenv("MAMBA_SS_FWD_WIDE")) wide = atoi(env) != 0;  // tests force it
+  wide = wide && dstate == 16 && p.n_seg == 1;
   // TMA needs 16-byte aligned bases and row strides (L * esize).
   p.tma_ok = (p.seqlen * esize) % 16 == 0 && aligned16(p.u) && aligned16(p.delta) &&
              aligned16(p.B) && aligned16(p.C) && (!p.z || aligned16(p.z));
@@ -649,7 +673,8 @@ cudaError_t launch_fwd(const FwdParams& p_in, int dstate, int io_dtype, int zoh,
   if (p.tma_ok) {
     const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
     const uint64_t brows = static_cast<uint64_t>(p.batch) * dstate;
-    const uint32_t ch = static_cast<uint32_t>(fwd_channels_per_cta(dstate));
+    const uint32_t ch = static_cast<uint32_t>(wide ? FwdCfg<16, true>::kCh
+                                                    : fwd_channels_per_cta(dstate));
     const uint64_t L = p.seqlen;
     p.tma_ok = encode_rows(&maps.d, p.delta, io_dtype, rows, L, ch) &&
                encode_rows(&maps.u, p.u, io_dtype, rows, L, ch) &&
@@ -658,11 +683,11 @@ cudaError_t launch_fwd(const FwdParams& p_in, int dstate, int io_dtype, int zoh,
                encode_rows(&maps.c, p.C, io_dtype, brows, L, dstate, io_dtype == MSS_F32);
   }
   if (io_dtype == MSS_BF16) {
-    return zoh ? launch_fwd_n<__nv_bfloat16, true>(p, maps, dstate, stream)
-               : launch_fwd_n<__nv_bfloat16, false>(p, maps, dstate, stream);
+    return zoh ? launch_fwd_n<__nv_bfloat16, true>(p, maps, dstate, wide, stream)
+               : launch_fwd_n<__nv_bfloat16, false>(p, maps, dstate, wide, stream);
   }
-  return zoh ? launch_fwd_n<float, true>(p, maps, dstate, stream)
-             : launch_fwd_n<float, false>(p, maps, dstate, stream);
+  return zoh ? launch_fwd_n<float, true>(p, maps, dstate, wide, stream)
+             : launch_fwd_n<float, false>(p, maps, dstate, wide, stream);
 }
 
 unsigned int take_fwd_device_error() {
