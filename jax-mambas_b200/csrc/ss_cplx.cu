@@ -36,12 +36,40 @@ struct CplxCfg {
   static constexpr int kThreads = kWarps * 32;
 };
 
-// (cos x, sin x), accurate: the state of a slowly decaying complex mode
-// accumulates the rounding of every step, so the fast SFU forms are not used
+// (cos x, sin x) to about one ulp for |x| up to 2^20, in straight-line code
+// (no large-argument path): Cody-Waite reduction x = k pi/2 + r, |r| <= pi/4,
+// with pi/2 split into three floats (P1 + P2 + P3, each the float nearest the
+// remainder) applied by fused multiply-adds, then the Taylor series of sin and
+// cos about 0 through r^9 and r^10 (truncation below 1e-9 on |r| <= pi/4), and
+// the quadrant k mod 4 choosing signs and order. The state of a slowly
+// decaying complex mode accumulates the rounding of every step, so the SFU's
+// approximate sin/cos are not used.
 __device__ __forceinline__ float2 cis(float x) {
-  float s, c;
-  sincosf(x, &s, &c);
-  return make_float2(c, s);
+  constexpr float kTwoOverPi = 0x1.45f306p-1f;
+  constexpr float kP1 = 0x1.921fb6p+0f, kP2 = -0x1.777a5cp-25f, kP3 = -0x1.ee59dap-50f;
+  const float kf = rintf(x * kTwoOverPi);
+  float r = fmaf(-kf, kP1, x);
+  r = fmaf(-kf, kP2, r);
+  r = fmaf(-kf, kP3, r);
+  const int k = static_cast<int>(kf);
+  const float r2 = r * r;
+  // sin r = r (1 - r^2/3! + r^4/5! - r^6/7! + r^8/9!)
+  float ps = fmaf(r2, 1.f / 362880.f, -1.f / 5040.f);
+  ps = fmaf(ps, r2, 1.f / 120.f);
+  ps = fmaf(ps, r2, -1.f / 6.f);
+  const float sr = fmaf(ps * r2, r, r);
+  // cos r = 1 - r^2/2! + r^4/4! - r^6/6! + r^8/8! - r^10/10!
+  float pc = fmaf(r2, -1.f / 3628800.f, 1.f / 40320.f);
+  pc = fmaf(pc, r2, -1.f / 720.f);
+  pc = fmaf(pc, r2, 1.f / 24.f);
+  pc = fmaf(pc, r2, -0.5f);
+  const float cr = fmaf(pc, r2, 1.f);
+  // quadrant: (cos, sin) of k pi/2 + r
+  const bool swap = (k & 1) != 0;
+  float c = swap ? sr : cr, sn = swap ? cr : sr;
+  if (((k + 1) & 2) != 0) c = -c;
+  if ((k & 2) != 0) sn = -sn;
+  return make_float2(c, sn);
 }
 
 struct Cx {
@@ -62,7 +90,7 @@ __device__ __forceinline__ void cdisc(float dl, Cx A, Cx& a, Cx& bb) {
   a = {m * cs.x, m * cs.y};
   if constexpr (kZOH) {
     // expm1(x + iy) = expm1(x) cos y - 2 sin^2(y/2) + i e^x sin y, over A
-    const float sh = sinf(0.5f * dl * A.i);
+    const float sh = cis(0.5f * dl * A.i).y;
     const Cx e1 = {fmaf(expm1f(dl * A.r), cs.x, -2.f * sh * sh), m * cs.y};
     const float den = A.r * A.r + A.i * A.i;
     bb = {(e1.r * A.r + e1.i * A.i) / den, (e1.i * A.r - e1.r * A.i) / den};
@@ -71,10 +99,11 @@ __device__ __forceinline__ void cdisc(float dl, Cx A, Cx& a, Cx& bb) {
   }
 }
 
+template <int kCh>
 struct CplxShared {
-  float dlt[8 * 4][kCRow];  // delta_eff (rows = channels of the CTA, up to 32)
-  float uu[8 * 4][kCRow];   // u (masked)
-  float yy[8 * 4][kCRow];   // forward: D u, then + y; backward: dy
+  float dlt[kCh][kCRow];  // delta_eff (rows = channels of the CTA)
+  float uu[kCh][kCRow];   // u (masked)
+  float yy[kCh][kCRow];   // forward: D u, then + y; backward: dy
   float2 Bt[16][kCT];
   float2 Ct[16][kCT];
 };
@@ -84,7 +113,7 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
     ss_cfwd_kernel(const CplxParams p) {
   using Cfg = CplxCfg<NS>;
   constexpr int kS = Cfg::kS, kLPC = Cfg::kLPC, kCh = Cfg::kCh, kThreads = Cfg::kThreads;
-  __shared__ CplxShared sh;
+  __shared__ CplxShared<kCh> sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y, d0 = blockIdx.x * kCh;
   const int L = p.seqlen;
@@ -131,36 +160,32 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
       sh.Ct[n][tt] = v ? C2[static_cast<size_t>(n) * L + t] : make_float2(0.f, 0.f);
     }
     __syncthreads();
-    // ---- scan
-    const int steps = min(kCT, len - t0);
-    for (int tt = 0; tt < steps; tt += 4) {
-      float yp[4] = {0.f, 0.f, 0.f, 0.f};
+    // ---- scan, one step per iteration (rolled: the per-step body is long);
+    // steps past the valid length carry delta = 0 and leave the state as is
+    const int steps4 = (min(kCT, len - t0) + 3) & ~3;
+#pragma unroll 1
+    for (int tt = 0; tt < steps4; ++tt) {
+      const float dl = sh.dlt[cl][tt];
+      const float uv = sh.uu[cl][tt];
+      const float dlu = dl * uv;
+      float yp = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float dl = sh.dlt[cl][tt + e];
-        const float uv = sh.uu[cl][tt + e];
-#pragma unroll
-        for (int j = 0; j < kS; ++j) {
-          const int n = q + kLPC * j;
-          Cx a, bb;
-          cdisc<kZOH>(dl, Av[j], a, bb);
-          const Cx Bn = cld(&sh.Bt[n][tt + e]);
-          const Cx bu = cmul(bb, {Bn.r * uv, Bn.i * uv});
-          const Cx ah = cmul(a, h[j]);
-          h[j] = {ah.r + bu.r, ah.i + bu.i};
-          const Cx Cn = cld(&sh.Ct[n][tt + e]);
-          yp[e] = fmaf(Cn.r, h[j].r, fmaf(-Cn.i, h[j].i, yp[e]));
-        }
+      for (int j = 0; j < kS; ++j) {
+        const int n = q + kLPC * j;
+        Cx a, bb;
+        cdisc<kZOH>(dl, Av[j], a, bb);
+        const Cx Bn = cld(&sh.Bt[n][tt]);
+        // Euler: b_bar u = delta u B (real times complex)
+        const Cx bu = kZOH ? cmul(bb, {Bn.r * uv, Bn.i * uv}) : Cx{dlu * Bn.r, dlu * Bn.i};
+        h[j] = {fmaf(a.r, h[j].r, fmaf(-a.i, h[j].i, bu.r)),
+                fmaf(a.r, h[j].i, fmaf(a.i, h[j].r, bu.i))};
+        const Cx Cn = cld(&sh.Ct[n][tt]);
+        yp = fmaf(Cn.r, h[j].r, fmaf(-Cn.i, h[j].i, yp));
       }
 #pragma unroll
-      for (int m = 1; m < kLPC; m <<= 1)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) yp[e] += __shfl_xor_sync(0xffffffffu, yp[e], m);
-      if (q == 0) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sh.yy[cl][tt + e] += yp[e];
-      }
-      if (act) {  // carry after these 4 steps, natural state order, complex
+      for (int m = 1; m < kLPC; m <<= 1) yp += __shfl_xor_sync(0xffffffffu, yp, m);
+      if (q == 0) sh.yy[cl][tt] += yp;
+      if (act && (tt & 3) == 3) {  // carry after each 4 steps, natural state order
         float2* cs = static_cast<float2*>(p.chunk_states) +
                      carry_offset(b, (t0 + tt) / kCkpt, p.n_chunks, p.dim, d, NS);
 #pragma unroll
@@ -191,12 +216,12 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
 }
 
 template <int NS, bool kZOH>
-__global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
+__global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads == 32 ? 11 : 1)
     ss_cbwd_kernel(const CplxParams p) {
   using Cfg = CplxCfg<NS>;
   constexpr int kS = Cfg::kS, kLPC = Cfg::kLPC, kCh = Cfg::kCh, kThreads = Cfg::kThreads;
   static_assert(Cfg::kWarps == 1, "the channel sums of dB / dC are per warp");
-  __shared__ CplxShared sh;
+  __shared__ CplxShared<kCh> sh;
   // one group's dB (re, im) and dC (re, im) per (channel, swizzled state),
   // summed over the warp's channels by flush_part
   __shared__ float4 part[4][kCh][NS];
@@ -300,14 +325,18 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float dl = sh.dlt[cl][tg + e], uv = sh.uu[cl][tg + e];
+        const float dlu = dl * uv;
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
           const int n = q + kLPC * j;
           cdisc<kZOH>(dl, Av[j], aa[e][j], bbv[e][j]);
           const Cx Bn = cld(&sh.Bt[n][tg + e]);
-          const Cx bu = cmul(bbv[e][j], {Bn.r * uv, Bn.i * uv});
-          const Cx ah = cmul(aa[e][j], hh[e][j]);
-          hh[e + 1][j] = {ah.r + bu.r, ah.i + bu.i};
+          const Cx bu =
+              kZOH ? cmul(bbv[e][j], {Bn.r * uv, Bn.i * uv}) : Cx{dlu * Bn.r, dlu * Bn.i};
+          const Cx& a = aa[e][j];
+          const Cx& hp = hh[e][j];
+          hh[e + 1][j] = {fmaf(a.r, hp.r, fmaf(-a.i, hp.i, bu.r)),
+                          fmaf(a.r, hp.i, fmaf(a.i, hp.r, bu.i))};
         }
       }
       float sB[4], sA[4];  // per step: sum_n Re(G conj(B)) (ZOH: Re(G conj(bb B))), sum_n Re(G conj(h) conj(A a))
@@ -328,7 +357,8 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
           // dC = dy conj(h_t), dB = G conj(bb) u
           const Cx ht = hh[e + 1][j];
           const Cx dCv = {dy * ht.r, -dy * ht.i};
-          const Cx gbb = cmulc(Gt, bbv[e][j]);
+          // Euler: G conj(bb) u = G delta u
+          const Cx gbb = kZOH ? cmulc(Gt, bbv[e][j]) : Cx{Gt.r * dl, Gt.i * dl};
           const Cx dBv = {gbb.r * uv, gbb.i * uv};
           {
             const int col = n ^ part_swz<NS>(cl);
