@@ -289,7 +289,7 @@ def run_gpu(args, cfg):
     mufu_bwd = elems * valid * mufu_b / (bwd_ms * 1e-3)
     mufu_fwd = elems * valid * mufu_f / (fwd_ms * 1e-3)
     traffic = args.traffic
-    if traffic is None and args.config == "c1":
+    if traffic is None and args.config == "c1" and not args.batch:
         tf = ROOT / "profiles" / "ncu_traffic.json"
         if tf.exists():
             traffic = json.loads(tf.read_text()).get("c1", {}).get("ss_bwd_tile_kernel")
@@ -754,6 +754,8 @@ def main():
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU in place of the config's (small profiling cases)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per backward launch, if captured")
     args = ap.parse_args()
@@ -768,6 +770,8 @@ def main():
              "block": run_block_bench, "c3": run_block_bench}[args.config](args)
         return
     cfg = CONFIGS[args.config]
+    if args.batch:
+        cfg = dict(cfg, batch=args.batch, workload=cfg["workload"] + f" (batch overridden: {args.batch})")
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

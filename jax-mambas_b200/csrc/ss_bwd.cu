@@ -188,8 +188,12 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, 
 
 // kSeg: the launch is cut into time segments (blockIdx.z); without it the
 // segment bounds are compile-time constants (one segment of the whole row).
-template <int NS, typename T, bool kZOH, bool kSeg>
-__global__ void __launch_bounds__(32)
+// kLPT: right-padded batches, grid rows take the sequences longest first
+// (batch_of_row); its bound of 16 CTAs per SM keeps the registers at the plain
+// kernel's 128 (the ranking code otherwise lifts them to ~170 and halves the
+// residency). 0 leaves the bound to the compiler.
+template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false>
+__global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
   using Cfg = TileCfg<NS>;
   using Sh = TileShared<NS, T>;
@@ -200,7 +204,8 @@ __global__ void __launch_bounds__(32)
   Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
 
   const int lane = threadIdx.x;
-  const int b = blockIdx.y;
+  const int b = kLPT ? batch_of_row(p.seq_lens, p.batch, p.seqlen, static_cast<int>(blockIdx.y))
+                     : static_cast<int>(blockIdx.y);
   const int d0 = blockIdx.x * kCh;
   const int L = p.seqlen;
   const int n_ch = min(kCh, p.dim - d0);
@@ -950,6 +955,10 @@ static cudaError_t launch_bwd_tile_t(const BwdParams& p, const TileMaps& maps,
   using Sh = TileShared<NS, T>;
   const size_t smem = offsetof(Sh, barP) + sizeof(uint64_t);
   auto kern = ss_bwd_tile_kernel<NS, T, kZOH, false>;
+  if constexpr (NS == 16 && !kZOH) {
+    if (p.seq_lens != nullptr && p.n_seg == 1 && p.batch <= kLongestFirstMax)
+      kern = ss_bwd_tile_kernel<NS, T, kZOH, false, true>;
+  }
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;

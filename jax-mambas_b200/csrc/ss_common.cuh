@@ -38,6 +38,34 @@ __device__ __forceinline__ size_t carry_offset(int b, int idx, int n_chunks, int
 }
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Batch index of the CTAs in grid row y. With per-sequence valid lengths
+// (right padding) a CTA's work is proportional to its sequence's valid
+// length, and CTAs are dispatched in grid order, so the rows run longest
+// sequence first (ties by index): the short CTAs fill the last wave instead
+// of a long one setting the tail. Every lane of the calling warp must be
+// present; batches beyond kLongestFirstMax keep the grid order.
+constexpr int kLongestFirstMax = 128;
+__device__ __forceinline__ int batch_of_row(const int32_t* seq_lens, int batch, int L, int y) {
+  if (seq_lens == nullptr || batch > kLongestFirstMax) return y;
+  const int lane = threadIdx.x & 31;
+  for (int base = 0; base < batch; base += 32) {
+    const int bb = base + lane;
+    bool hit = false;
+    if (bb < batch) {
+      const int lb = max(0, min(L, __ldg(seq_lens + bb)));
+      int rank = 0;
+      for (int o = 0; o < batch; ++o) {
+        const int lo = max(0, min(L, __ldg(seq_lens + o)));
+        rank += (lo > lb || (lo == lb && o < bb)) ? 1 : 0;
+      }
+      hit = rank == y;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (m != 0u) return base + __ffs(static_cast<int>(m)) - 1;
+  }
+  return y;
+}
+
 struct FwdParams {
   int batch, dim, seqlen, n_chunks;  // n_chunks: saved carries per row, ceil(L / kCkpt)
   int delta_softplus;

@@ -109,7 +109,9 @@ __device__ __forceinline__ void store4_global(__nv_bfloat16* dst, const float (&
 
 // kEnd: the end-state pass of a segmented scan (no outputs; each segment from
 // a zero state, its final state and sum of delta_eff to seg_end / seg_dsum).
-template <int NS, typename T, bool kZOH, bool kEnd, bool kWide>
+// kLPT: right-padded batches, grid rows take the sequences longest first
+// (batch_of_row).
+template <int NS, typename T, bool kZOH, bool kEnd, bool kWide, bool kLPT = false>
 __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     ss_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   using Cfg = FwdCfg<NS, kWide>;
@@ -128,7 +130,8 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int b = blockIdx.y;
+  const int b = kLPT ? batch_of_row(p.seq_lens, p.batch, p.seqlen, static_cast<int>(blockIdx.y))
+                     : static_cast<int>(blockIdx.y);
   const int d0 = blockIdx.x * kCh;
   const int L = p.seqlen;
   const int n_ch = min(kCh, p.dim - d0);  // live channels of this CTA
@@ -542,6 +545,12 @@ __global__ void seg_combine_fwd_kernel(const float* __restrict__ A, const float*
   }
 }
 
+// Whether the grid rows take the batches longest first (right padding, one
+// time segment).
+static bool longest_first(const FwdParams& p) {
+  return p.seq_lens != nullptr && p.n_seg == 1 && p.batch <= kLongestFirstMax;
+}
+
 template <int NS, typename T, bool kZOH>
 static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps, bool wide,
                                 cudaStream_t stream) {
@@ -549,7 +558,8 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps, bool wi
     if (wide) {  // unsegmented only
       using CfgW = FwdCfg<NS, true>;
       const size_t smem_w = sizeof(FwdShared<NS, T, true>);
-      auto kern_w = ss_fwd_kernel<NS, T, kZOH, false, true>;
+      auto kern_w = longest_first(p) ? ss_fwd_kernel<NS, T, kZOH, false, true, true>
+                                     : ss_fwd_kernel<NS, T, kZOH, false, true>;
       cudaError_t e = cudaFuncSetAttribute(
           kern_w, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_w));
       if (e != cudaSuccess) return e;
@@ -561,6 +571,9 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps, bool wi
   using Cfg = FwdCfg<NS>;
   const size_t smem = sizeof(FwdShared<NS, T>);
   auto kern = ss_fwd_kernel<NS, T, kZOH, false, false>;
+  if constexpr (NS == 16) {
+    if (longest_first(p)) kern = ss_fwd_kernel<NS, T, kZOH, false, false, true>;
+  }
   auto kern_end = ss_fwd_kernel<NS, T, kZOH, true, false>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
