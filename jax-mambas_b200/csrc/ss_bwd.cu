@@ -109,11 +109,15 @@ __device__ __forceinline__ int grp_off(const __nv_bfloat16*, int key, int g) {
 __device__ __forceinline__ float4 ld4p(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
+// bf16 -> fp32 is exact: the bf16 bits are the fp32's upper half. Two
+// integer operations per pair (a shift for the low element, a mask for the
+// high one).
+__device__ __forceinline__ float4 bf16x4_to_f32(uint2 w) {
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
+                     __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+}
 __device__ __forceinline__ float4 ld4p(const __nv_bfloat16* p) {
-  const uint2 w = *reinterpret_cast<const uint2*>(p);
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-  return make_float4(a.x, a.y, b.x, b.y);
+  return bf16x4_to_f32(*reinterpret_cast<const uint2*>(p));
 }
 
 // Steps t .. t+3 (t a multiple of 4) of row r as fp32.
@@ -121,10 +125,7 @@ __device__ __forceinline__ float4 ld4s(const float* tile, int r, int t) {
   return *reinterpret_cast<const float4*>(tile + sw_idx(tile, r, t));
 }
 __device__ __forceinline__ float4 ld4s(const __nv_bfloat16* tile, int r, int t) {
-  const uint2 w = *reinterpret_cast<const uint2*>(tile + sw_idx(tile, r, t));
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-  return make_float4(a.x, a.y, b.x, b.y);
+  return bf16x4_to_f32(*reinterpret_cast<const uint2*>(tile + sw_idx(tile, r, t)));
 }
 __device__ __forceinline__ void st4s(float* tile, int r, int t, float4 v) {
   *reinterpret_cast<float4*>(tile + sw_idx(tile, r, t)) = v;
