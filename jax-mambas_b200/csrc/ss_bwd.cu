@@ -109,13 +109,6 @@ __device__ __forceinline__ int grp_off(const __nv_bfloat16*, int key, int g) {
 __device__ __forceinline__ float4 ld4p(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
-// bf16 -> fp32 is exact: the bf16 bits are the fp32's upper half. Two
-// integer operations per pair (a shift for the low element, a mask for the
-// high one).
-__device__ __forceinline__ float4 bf16x4_to_f32(uint2 w) {
-  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
-                     __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
-}
 __device__ __forceinline__ float4 ld4p(const __nv_bfloat16* p) {
   return bf16x4_to_f32(*reinterpret_cast<const uint2*>(p));
 }

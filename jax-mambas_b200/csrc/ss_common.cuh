@@ -202,6 +202,16 @@ struct StepParams {
 };
 
 // ---------------------------------------------------------------- typed I/O
+// bf16 -> fp32 is exact: the bf16 bits are the fp32's upper half, so the
+// widening is a shift (low element of a pair) or a mask (high element).
+__device__ __forceinline__ float bf16_bits_to_f32(unsigned short h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+__device__ __forceinline__ float4 bf16x4_to_f32(uint2 w) {
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
+                     __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+}
+
 template <typename T>
 struct Elem;
 
@@ -214,7 +224,7 @@ struct Elem<float> {
 template <>
 struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float ld(const __nv_bfloat16* p) {
-    return __bfloat162float(__ldg(p));
+    return bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p)));
   }
   static __device__ __forceinline__ void st(__nv_bfloat16* p, float v) {
     *p = __float2bfloat16_rn(v);
@@ -222,7 +232,9 @@ struct Elem<__nv_bfloat16> {
 };
 
 __device__ __forceinline__ float to_f32(float v) { return v; }
-__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) {
+  return bf16_bits_to_f32(__bfloat16_as_ushort(v));
+}
 
 // ------------------------------------------------------------- activations
 // 2^x on the special-function unit.

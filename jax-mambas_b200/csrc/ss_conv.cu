@@ -35,10 +35,8 @@ __device__ __forceinline__ void load4_row(const T* row, int t, int lim, bool vec
       const float4 f = *reinterpret_cast<const float4*>(row + t);
       v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
     } else {
-      const uint2 w = *reinterpret_cast<const uint2*>(row + t);
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+      const float4 f = bf16x4_to_f32(*reinterpret_cast<const uint2*>(row + t));
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
     }
   } else {
 #pragma unroll

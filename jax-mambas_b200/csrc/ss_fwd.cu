@@ -92,10 +92,8 @@ __device__ __forceinline__ void load4_smem(const float* src, float (&v)[4]) {
   v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
 }
 __device__ __forceinline__ void load4_smem(const __nv_bfloat16* src, float (&v)[4]) {
-  const uint2 w = *reinterpret_cast<const uint2*>(src);
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  const float4 f = bf16x4_to_f32(*reinterpret_cast<const uint2*>(src));
+  v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
 }
 __device__ __forceinline__ void store4_global(float* dst, const float (&v)[4]) {
   *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
