@@ -202,13 +202,15 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     if (!kEnd) tma_load_2d(&sh.rawC[s][0][0], &maps.c, t0, b * NS, bar);
   };
 
-  // transform / emit items (4 steps of one channel): lane tid takes steps
-  // (tid % 8) * 4 .. + 3 of channels tid / 8 + k * kItemChStride
+  // transform / emit items (4 steps of one channel): lane l of warp w takes
+  // steps (l % 8) * 4 .. + 3 of channels w kCPW + l / 8 + k * kItemChStride,
+  // i.e. only its own warp's scan channels, so that the work rows pass from
+  // transform to scan to emit within the warp
   constexpr int kItems = kCh * (kTile / 4) / kThreads;
-  constexpr int kItemChStride = kThreads / (kTile / 4);
-  static_assert(kItems * kItemChStride == kCh, "items cover the channels");
-  const int it_tt = (tid % (kTile / 4)) * 4;
-  const int it_c0 = tid / (kTile / 4);
+  constexpr int kItemChStride = 32 / (kTile / 4);
+  static_assert(kItems * kItemChStride == Cfg::kCPW, "a warp's items cover its channels");
+  const int it_tt = (lane % (kTile / 4)) * 4;
+  const int it_c0 = warp * Cfg::kCPW + lane / (kTile / 4);
   float it_bias[kItems], it_D[kItems];
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
@@ -232,11 +234,9 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     const int s = kk & 1;
     const int t0 = k * kTile;
     if (use_tma) {
-      if (tid == 0 && k + 1 < k_end) {
-        fence_proxy_async_smem();  // the previous reads of that buffer are done
-        issue(k + 1);
-      }
       const bool ok = mbar_wait_bounded(&sh.bar[s], (kk >> 1) & 1);
+      // the CTA's one barrier per tile (TMA staging): past it every warp is
+      // done with the previous tile, whose staging buffer the next copies fill
       if (__syncthreads_or(!ok)) {
         // A copy never completed: report it, let the in-flight copies of the
         // other buffer finish (bounded), and leave.
@@ -246,7 +246,14 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
         }
         return;
       }
+      if (tid == 0 && k + 1 < k_end) {
+        fence_proxy_async_smem();  // the previous tile's reads of that buffer are done
+        issue(k + 1);
+      }
     }
+    // fp32 B/C read in place from the TMA staging: no CTA-wide widening, and
+    // the transform, scan and emit of a channel stay in one warp
+    const bool lean = kDirectBC && use_tma;
 
     // whole tile: every channel live, every step valid, staged by TMA; the
     // transform and emit then run without per-element predicates
@@ -325,7 +332,11 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
           }
         }
       }
-      __syncthreads();
+      if (lean) {
+        __syncwarp();
+      } else {
+        __syncthreads();  // B/C widened by the whole CTA
+      }
 
       // ---- 2. sequential scan over the tile, 4 steps per iteration; the
       // kLPC lanes of a channel read adjacent B/C rows (distinct banks) and
@@ -444,7 +455,7 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
       }
     }
 
-    __syncthreads();
+    __syncwarp();  // the warp's y rows
 
     if constexpr (!kEnd) {
       // ---- 3. emit out = (y + D u) * silu(z), and y + D u, 4 steps per item
@@ -501,7 +512,9 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
         emit(std::false_type{});
       }
     }
-    __syncthreads();
+    // with TMA the next tile's barrier follows its wait; plain staging keeps
+    // the widened B/C of this tile until every warp has scanned it
+    if (!use_tma) __syncthreads();
   }
 
   if constexpr (kEnd) {
