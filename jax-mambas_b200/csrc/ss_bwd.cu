@@ -184,8 +184,8 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, 
 // segment bounds are compile-time constants (one segment of the whole row).
 // kLPT: right-padded batches, grid rows take the sequences longest first
 // (batch_of_row); its bound of 16 CTAs per SM keeps the registers at the plain
-// kernel's 128 (the ranking code otherwise lifts them to ~170 and halves the
-// residency). 0 leaves the bound to the compiler.
+// kernel's 128 (the ranking code otherwise lifts them to ~170, which cuts the
+// resident warps per SM from 16 to 12). 0 leaves the bound to the compiler.
 template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false>
 __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
