@@ -101,7 +101,7 @@ SIGNATURES = {
         [_c_void_p, _i32, _i32, _i32, _i32, _i32, _i32]
         + [_c_void_p] * 8  # u delta A B C D z delta_bias
         + [_i32]  # delta_softplus
-        + [_c_void_p] * 14,  # initial_state seq_lens chunk_states out_pre dout dlast du ddelta dA dB dC dD dz dbias dinit
+        + [_c_void_p] * 15,  # initial_state seq_lens chunk_states out_pre dout dlast du ddelta dA dB dC dD dz dbias dinit
     ),
 }
 
