@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, rel_err, to_dev
+from _helpers import assert_bf16_close, BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, rel_err, to_dev
 from oracle import selective_scan_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -96,7 +96,7 @@ def test_bf16(L):
     res = _run(x, w, b, seq, st, du, io=torch.bfloat16)
     ref = _ref(xr, w, b, seq, str_, bf16_round(du))
     for k in ("u", "final", "dx", "dw", "db", "dstate"):
-        assert rel_err(res[k], ref[k]) < BF16_TOL, k
+        assert_bf16_close(res[k], ref[k], k)
 
 
 def test_rejects_bad_arguments():

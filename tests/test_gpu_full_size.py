@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import BF16_TOL, BWD_TOL, FWD_TOL, assert_close, rel_err
+from _helpers import assert_bf16_close, BF16_TOL, BWD_TOL, FWD_TOL, assert_close, rel_err
 from oracle import selective_scan_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -70,7 +70,7 @@ def _check(x, res, ch, tol_fwd, tol_bwd, bf16):
     for k, v in sel.items():
         a = v.float().cpu().numpy()
         if bf16:
-            assert rel_err(a, ref[k]) < BF16_TOL, k
+            assert_bf16_close(a, ref[k], k)
         else:
             assert_close(a, ref[k], tol_fwd if k in ("out", "last_state") else tol_bwd, k)
 

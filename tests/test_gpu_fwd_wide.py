@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, oracle_fused, \
+from _helpers import assert_bf16_close, BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, oracle_fused, \
     rel_err, run_fused
 from oracle import selective_scan_oracle as orc
 
@@ -55,7 +55,7 @@ def test_bf16_padded(wide):
     res = run_fused(x, io_dtype=torch.bfloat16)
     ref = oracle_fused(x, io_round=bf16_round)
     for k in ("out", "last_state", "du", "ddelta", "dA", "dB", "dC", "dD", "dz", "ddelta_bias"):
-        assert rel_err(res[k], ref[k]) < BF16_TOL, k
+        assert_bf16_close(res[k], ref[k], k)
     for b, n in enumerate(x["seq_lens"]):
         assert np.all(res["out"][b, :, n:] == 0.0)
 

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import (BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, oracle_fused,
+from _helpers import (assert_bf16_close, BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, oracle_fused,
                       rel_err)
 from oracle import selective_scan_oracle as orc
 
@@ -57,10 +57,10 @@ def test_pipeline_bf16_padded_no_z():
     x = orc.make_inputs(6, 24, 512, 16, seed=61, with_z=False, valid_lengths=(100, 512))
     ref = oracle_fused(x, io_round=bf16_round)
     res = _run(x, torch.bfloat16, 2, 2, with_z=False)
-    assert rel_err(res["out"], ref["out"]) < BF16_TOL
+    assert_bf16_close(res["out"], ref["out"])
     for k, r in _KEYS.items():
         if k != "dz":
-            assert rel_err(res[k], ref[r]) < BF16_TOL, k
+            assert_bf16_close(res[k], ref[r], k)
     # padding positions are exact zeros
     for b, n in enumerate(x["seq_lens"]):
         assert not res["out"][b, :, n:].any()

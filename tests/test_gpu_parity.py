@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import (BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round,
+from _helpers import (assert_bf16_close, BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round,
                       oracle_fused, rel_err, run_fused, to_dev)
 from oracle import selective_scan_oracle as orc
 
@@ -69,10 +69,10 @@ def test_bf16_io(aligned):
     x = orc.make_inputs(2, 16, L, 16, seed=3)
     res = run_fused(x, io_dtype=torch.bfloat16)
     ref = oracle_fused(x, io_round=bf16_round)
-    assert rel_err(res["out"], ref["out"]) < BF16_TOL
-    assert rel_err(res["last_state"], ref["last_state"]) < BF16_TOL
+    assert_bf16_close(res["out"], ref["out"])
+    assert_bf16_close(res["last_state"], ref["last_state"])
     for k in ("du", "ddelta", "dA", "dB", "dC", "dD", "dz", "ddelta_bias"):
-        assert rel_err(res[k], ref[k]) < BF16_TOL, k
+        assert_bf16_close(res[k], ref[k], k)
 
 
 def test_padding_exact_zeros_and_state(monkeypatch):

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, oracle_fused, \
+from _helpers import assert_bf16_close, BF16_TOL, BWD_TOL, FWD_TOL, assert_close, bf16_round, oracle_fused, \
     rel_err, run_fused
 from oracle import selective_scan_oracle as orc
 
@@ -64,7 +64,7 @@ def test_bf16(segments):
     res = run_fused(x, io_dtype=torch.bfloat16)
     ref = oracle_fused(x, io_round=bf16_round)
     for k in ("out", "last_state", "du", "ddelta", "dA", "dB", "dC", "dD", "dz", "ddelta_bias"):
-        assert rel_err(res[k], ref[k]) < BF16_TOL, k
+        assert_bf16_close(res[k], ref[k], k)
 
 
 def test_padding(segments):

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from _helpers import BF16_TOL, FWD_TOL, assert_close, bf16_round, rel_err, to_dev
+from _helpers import assert_bf16_close, BF16_TOL, FWD_TOL, assert_close, bf16_round, rel_err, to_dev
 from oracle import selective_scan_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -54,8 +54,8 @@ def test_step_bf16():
     r = lambda k: bf16_round(x[k])
     ey, eh = orc.fused_step(x["state"], r("u"), r("delta"), x["A"], r("B"), r("C"), x["D"],
                             r("z"), x["bias"], True)
-    assert rel_err(out.float().cpu().numpy(), ey) < BF16_TOL
-    assert rel_err(st.cpu().numpy(), eh) < BF16_TOL
+    assert_bf16_close(out.float().cpu().numpy(), ey)
+    assert_bf16_close(st.cpu().numpy(), eh)
 
 
 def test_steps_reproduce_the_scan():
