@@ -1,13 +1,18 @@
 """Selective-scan fwd+bwd throughput on B200 (B*D*L Gelem/s) — the metric of
 BASELINE.json.
 
-Default workload: configs[1] — B=8, D=1536, L=2048, N=16, fp32, fused
-softplus(delta + bias), D skip and silu(z) gate, dy ~ N(0,1). One step = one
-forward + one backward of the fused selective scan over one batch (plus, for
-N>1 GPUs, the all-reduce of dA, dD and ddelta_bias across ranks: the batch is
-sharded, each rank holds a full configs[1] batch, i.e. weak scaling).
-``--config c2`` runs configs[2] (bf16 I/O, B=16, D=5120, L=4096, right-padded
-valid lengths ~ U[512, 4096]).
+Default workload: configs[2], the Mamba-2.8B layer shape the target is quoted
+on — B=16, D=5120, L=4096, N=16, bf16 u/delta/z/B/C with fp32 A, D, bias and
+state, fused softplus(delta + bias), D skip and silu(z) gate, dy ~ N(0,1),
+right-padded valid lengths ~ U[512, 4096] (delta = u = 0 past them). One step
+= one forward + one backward of the fused selective scan over one batch (plus,
+for N>1 GPUs, the all-reduce of dA, dD and ddelta_bias across ranks: the
+batch is sharded, each rank holds a full configs[2] batch, i.e. weak
+scaling). ``value`` counts valid (sequence, channel, step) positions per
+second; ``value_all_positions`` counts every B*D*L position.
+The line also carries ``channel_sharded``: configs[4]'s single sequence
+(B=1, L=131072, D=5120, bf16) with d_inner split over the N ranks (strong
+scaling). ``--config c1`` runs configs[1] (fp32, B=8, D=1536, L=2048).
 
 ``--impl reference`` times the reference's CPU path instead: JAX is not
 installed on this image, so it runs the NumPy restatement of the reference's
@@ -151,13 +156,210 @@ class _stdout_to_stderr:
         os.close(self._saved)
 
 
+def _seq_lens(cfg, rank, world):
+    """This rank's valid lengths for a right-padded config: the global batch's
+    lengths ~ U[512, L] from one seeded generator (the same draw on every
+    rank), dealt to the ranks token-balanced (longest first, snake order), as
+    a length-aware data loader would. Returns (lengths of this rank, lengths
+    of the global batch), int32 CPU tensors."""
+    import torch
+
+    from mamba.distributed import token_balanced_shards
+
+    b, L = cfg["batch"], cfg["length"]
+    g = torch.Generator()
+    g.manual_seed(4321)
+    lens = torch.randint(512, L + 1, (b * world,), generator=g, dtype=torch.int32)
+    idx = token_balanced_shards(lens.tolist(), world)[rank]
+    return lens[idx].contiguous(), lens
+
+
+class ScanCase:
+    """Device inputs and outputs of one rank's share of a config, and its step:
+    fused forward, fused backward, and the exchange (batch sharding: the
+    all-reduce of [dA | dD | ddelta_bias]; channel sharding: of dB and dC).
+
+    The exchange is issued asynchronously on NCCL's stream right after the
+    backward; only the next backward (which rewrites the reduced buffers)
+    waits for it, so it runs under the next step's forward."""
+
+    def __init__(self, cfg, rank, world, dev):
+        import torch
+
+        from mamba import selective_scan_cuda as ssc
+        from mamba.distributed import channel_shard, flat_param_grads
+
+        self.cfg, self.rank, self.world, self.dev = cfg, rank, world, dev
+        b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+        self.chan = cfg.get("shard") == "channels"
+        self.d_total = d
+        if self.chan:  # this rank's block of channels; B and C are shared
+            sl = channel_shard(d, rank, world)
+            d = sl.stop - sl.start
+        self.b, self.d, self.L, self.n = b, d, L, n
+        io = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+        self.io, self.esize = io, (2 if io == torch.bfloat16 else 4)
+        g = torch.Generator(device=dev)
+        g.manual_seed(1234 + (0 if self.chan else rank))
+
+        def normal(*shape):
+            return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(io)
+
+        self.u, self.delta, self.z, self.dout = (normal(b, d, L) for _ in range(4))
+        self.B, self.C = normal(b, n, L), normal(b, n, L)
+        self.A = (-torch.arange(1, n + 1, device=dev, dtype=torch.float32)).expand(d, n).contiguous()
+        self.Dp = torch.randn(d, generator=g, device=dev)
+        self.bias = torch.rand(d, generator=g, device=dev) * 2.0 - 4.0
+        self.seq_lens = None
+        self.valid_steps = b * L  # this rank's valid (sequence, step) pairs
+        self.valid_steps_global = b * L * (1 if self.chan else world)
+        if cfg["padded"]:
+            lens, all_lens = _seq_lens(cfg, rank, world)
+            self.seq_lens = lens.to(dev)
+            self.valid_steps = int(lens.sum())
+            self.valid_steps_global = int(all_lens.sum())
+            m = (torch.arange(L, device=dev)[None, :] < self.seq_lens[:, None].long())[:, None, :]
+            self.delta.masked_fill_(~m, 0)
+            self.u.masked_fill_(~m, 0)
+        self.out, self.pre = torch.empty_like(self.u), torch.empty_like(self.u)
+        self.last = torch.empty(b, d, n, device=dev)
+        self.cs = torch.empty(ssc.chunk_states_elems(b, L, d, n), device=dev)
+        self.du, self.ddl, self.dz = (torch.empty_like(self.u) for _ in range(3))
+        self.dB, self.dC = torch.empty_like(self.B), torch.empty_like(self.C)
+        self.params, self.dA, self.dDp, self.dbias = flat_param_grads(d, n, dev)
+        self.ws = ssc._alloc_workspace(b, L, d, n, 1 if io == torch.bfloat16 else 0, dev)
+        self.work = []
+        self.ssc = ssc
+
+    def fwd(self):
+        self.ssc.fused_forward_into(self.u, self.delta, self.A, self.B, self.C, self.Dp, self.z,
+                                    self.bias, True, None, self.seq_lens, self.out, self.last,
+                                    self.cs, out_pre=self.pre)
+
+    def bwd(self):
+        for w in self.work:  # the previous step's exchange reads the buffers rewritten here
+            w.wait()
+        self.work = []
+        self.ssc.fused_backward_into(self.u, self.delta, self.A, self.B, self.C, self.Dp, self.z,
+                                     self.bias, True, None, self.seq_lens, self.cs, self.dout,
+                                     None, self.du, self.ddl, self.dA, self.dB, self.dC,
+                                     self.dDp, self.dz, self.dbias, None, self.ws,
+                                     out_pre=self.pre)
+
+    def exchange(self):
+        from mamba.distributed import allreduce_bc_grads, allreduce_param_grads
+
+        if self.chan:
+            self.work = allreduce_bc_grads(self.dB, self.dC, async_op=True)
+        else:
+            w = allreduce_param_grads(self.params, async_op=True)
+            self.work = [w] if w is not None else []
+
+    def finish(self):
+        for w in self.work:
+            w.wait()
+        self.work = []
+
+    def step(self):
+        self.fwd()
+        self.bwd()
+        self.exchange()
+
+    def time(self, steps, warmup, sampler=None):
+        """(total ms over `steps`, mean forward ms, mean backward ms), CUDA
+        events on the launching stream; total is the max over ranks."""
+        import torch
+        import torch.distributed as dist
+
+        for _ in range(max(warmup, 0)):
+            self.step()
+        self.finish()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream(self.dev)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ctx = sampler if sampler is not None else _Null()
+        with ctx:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for i in range(steps):
+                ev[i][0].record(stream)
+                self.fwd()
+                ev[i][1].record(stream)
+                self.bwd()
+                ev[i][2].record(stream)
+                self.exchange()
+            self.finish()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier()
+        total = t0.elapsed_time(t1)
+        fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+        bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+        if self.world > 1:
+            t = torch.tensor([total], device=self.dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total = float(t.item())
+        return total, fwd_ms, bwd_ms
+
+    def launches_per_step(self):
+        """Kernels of this library per step: forward 1, backward 2 (tile +
+        parameter reduction), + 2 bf16 narrowings of dB/dC; time segments add
+        the end-state pass and its combine (forward) and the adjoint pass and
+        its combine (backward)."""
+        k = 3 + (2 if self.io.is_floating_point and self.esize == 2 else 0)
+        if self.ssc._lib().mamba_ss_segments(self.b, self.L, self.d, self.n) > 1:
+            k += 4
+        return k
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def _config_block(cfg, world):
+    """The line's ``config`` object (the same for the GPU and reference arms)."""
+    b, L, n = cfg["batch"], cfg["length"], cfg["dstate"]
+    chan = cfg.get("shard") == "channels"
+    d_rank = -(-cfg["dim"] // world) if chan else cfg["dim"]
+    esize = 2 if cfg["dtype"] == "bf16" else 4
+    valid = 1.0
+    if cfg["padded"]:
+        _, all_lens = _seq_lens(cfg, 0, world)
+        valid = float(all_lens.sum()) / (b * world * L)
+    return {"workload": cfg["workload"], "batch_per_gpu": b, "dim": cfg["dim"],
+            "dim_per_gpu": d_rank, "length": L, "dstate": n, "io_dtype": cfg["dtype"],
+            "global_batch": b * (1 if chan else world),
+            "parallelism": (f"channel-sharded over {world} GPUs" if chan
+                            else f"batch-sharded dp{world}") if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (u, delta, z, dy: "
+                  f"{b * d_rank * L * esize * 4 / 1e6:.0f} MB per step)",
+            "valid_fraction": round(valid, 4),
+            "valid_lengths": "U[512, L], global batch dealt to ranks token-balanced"
+            if cfg["padded"] else None,
+            "value_counts": "valid (sequence, channel, step) positions"}
+
+
+def _ncu_counts(config):
+    """Per valid element DRAM bytes and warp instructions of each scan kernel
+    for `config`, from a committed ncu capture summary (profiles/)."""
+    f = ROOT / "profiles" / "ncu_counts.json"
+    if not f.exists():
+        return None
+    return json.loads(f.read_text()).get(config)
+
+
 def run_gpu(args, cfg):
     import torch
     import torch.distributed as dist
-
-    from mamba import selective_scan_cuda as ssc
-    from mamba.distributed import (allreduce_bc_grads, allreduce_param_grads, channel_shard,
-                                   flat_param_grads)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -171,140 +373,91 @@ def run_gpu(args, cfg):
             dist.init_process_group("nccl", device_id=dev)
             dist.barrier()
 
-    b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
-    chan = cfg.get("shard") == "channels"
-    d_total = d
-    if chan:  # this rank's block of channels; B and C are shared
-        sl = channel_shard(d, rank, world)
-        d = sl.stop - sl.start
-    io = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
-    esize = 2 if io == torch.bfloat16 else 4
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-
-    def normal(*shape):
-        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(io)
-
-    u, delta, z, dout = normal(b, d, L), normal(b, d, L), normal(b, d, L), normal(b, d, L)
-    Bm, Cm = normal(b, n, L), normal(b, n, L)
-    A = (-torch.arange(1, n + 1, device=dev, dtype=torch.float32)).expand(d, n).contiguous()
-    Dp = torch.randn(d, generator=g, device=dev)
-    bias = torch.rand(d, generator=g, device=dev) * 2.0 - 4.0
-    seq_lens = None
-    if cfg["padded"]:
-        seq_lens = torch.randint(512, L + 1, (b,), generator=g, device=dev, dtype=torch.int32)
-        t_idx = torch.arange(L, device=dev)
-        m = (t_idx[None, :] < seq_lens[:, None].long())[:, None, :]
-        delta.masked_fill_(~m, 0)
-        u.masked_fill_(~m, 0)
-
-    out = torch.empty_like(u)
-    pre = torch.empty_like(u)
-    last = torch.empty(b, d, n, device=dev)
-    cs = torch.empty(ssc.chunk_states_elems(b, L, d, n), device=dev)
-    du, ddl, dz = torch.empty_like(u), torch.empty_like(u), torch.empty_like(u)
-    dB, dC = torch.empty_like(Bm), torch.empty_like(Cm)
-    params, dA, dDp, dbias = flat_param_grads(d, n, dev)  # one all-reduce buffer
-    ws = ssc._alloc_workspace(b, L, d, n, 1 if io == torch.bfloat16 else 0, dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def fwd():
-        ssc.fused_forward_into(u, delta, A, Bm, Cm, Dp, z, bias, True, None, seq_lens,
-                               out, last, cs, out_pre=pre)
-
-    def bwd():
-        ssc.fused_backward_into(u, delta, A, Bm, Cm, Dp, z, bias, True, None, seq_lens, cs,
-                                dout, None, du, ddl, dA, dB, dC, dDp, dz, dbias, None, ws,
-                                out_pre=pre)
-
-    def exchange():
-        if chan:
-            allreduce_bc_grads(dB, dC)  # dB, dC sum over every channel
-        else:
-            allreduce_param_grads(params)  # dA, dD, ddelta_bias sum over sequences
-
-    def step():
-        fwd()
-        bwd()
-        exchange()
-
-    for _ in range(max(args.warmup, 0)):
-        step()
-    torch.cuda.synchronize()
-
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    case = ScanCase(cfg, rank, world, dev)
     sampler = ClockSampler(local)
-    with sampler:
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
-        for i in range(args.steps):
-            ev[i][0].record(stream)
-            fwd()
-            ev[i][1].record(stream)
-            bwd()
-            ev[i][2].record(stream)
-            exchange()
-        t_end.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    total_ms = t_start.elapsed_time(t_end)
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    total_ms, fwd_ms, bwd_ms = case.time(args.steps, args.warmup, sampler)
     clocks = sampler.summary()
-
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-
-    elems, fwd_bytes, bwd_bytes, carry_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize, d)
-    # padded steps are skipped by the kernels: the rooflines count
-    # the valid steps only, the headline value counts every B*D*L position
-    valid = 1.0
-    if seq_lens is not None:
-        valid = float(seq_lens.sum().item()) / (b * L)
-    fwd_bytes, bwd_bytes, carry_bytes = fwd_bytes * valid, bwd_bytes * valid, carry_bytes * valid
+    b, d, L, n, esize = case.b, case.d, case.L, case.n, case.esize
+    launches = case.launches_per_step() * args.steps
+    valid = case.valid_steps / (b * L)
     ms_per_step = total_ms / args.steps
-    total_elems = b * d_total * L if chan else elems * world
-    value = total_elems / (ms_per_step * 1e-3) / 1e9
+    # throughput counts valid positions only (padded steps are skipped by the
+    # kernels); the all-position figure is reported beside it
+    total_valid = case.valid_steps_global * case.d_total
+    total_all = b * L * case.d_total * (1 if case.chan else world)
+    value = total_valid / (ms_per_step * 1e-3) / 1e9
+    value_all = total_all / (ms_per_step * 1e-3) / 1e9
+    del case
+    torch.cuda.empty_cache()
+
+    # ---- strong scaling: configs[4]'s single sequence, channels over the ranks
+    strong = None
+    if args.strong and args.config != "c4":
+        c4 = ScanCase(CONFIGS["c4"], rank, world, dev)
+        s_ms, s_f, s_b = c4.time(max(3, min(args.steps, 10)), 3)
+        s_steps = max(3, min(args.steps, 10))
+        strong = {"workload": CONFIGS["c4"]["workload"], "scaling": "strong",
+                  "value": round(c4.b * c4.L * c4.d_total / (s_ms / s_steps * 1e-3) / 1e9, 3),
+                  "unit": UNIT, "ms_per_step": round(s_ms / s_steps, 3), "steps": s_steps,
+                  "dim_per_gpu": c4.d, "dtype": "bf16",
+                  "segments": int(c4.ssc._lib().mamba_ss_segments(c4.b, c4.L, c4.d, c4.n)),
+                  "kernels_ms": {"fwd": round(s_f, 3), "bwd": round(s_b, 3)},
+                  "exchange": "async NCCL all-reduce of dB and dC (sums over all channels)"}
+        launches += c4.launches_per_step() * s_steps
+        del c4
+        torch.cuda.empty_cache()
 
     # ---- e2e through the public API with host buffers
-    e2e = run_e2e(args, cfg, dev, io, rank, world) if args.e2e and not chan else None
+    e2e = run_e2e(args, cfg, dev, rank, world) if args.e2e and cfg.get("shard") != "channels" \
+        else None
 
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return None
 
+    elems, fwd_bytes, bwd_bytes, carry_bytes, mufu_f, mufu_b = _algorithmic(cfg, esize, d)
+    fwd_bytes, bwd_bytes, carry_bytes = fwd_bytes * valid, bwd_bytes * valid, carry_bytes * valid
+    valid_elems = elems * valid  # one launch's valid (sequence, channel, step) triples
     hbm, sm_max, peak_src = _peaks()
     bwd_gbs = bwd_bytes / (bwd_ms * 1e-3) / 1e9
     fwd_gbs = fwd_bytes / (fwd_ms * 1e-3) / 1e9
     f_mhz = clocks.get("sm_mhz") or sm_max
     mufu_peak = 148 * 16 * f_mhz * 1e6  # ops/s: 16 MUFU lanes per SM per clock
-    mufu_bwd = elems * valid * mufu_b / (bwd_ms * 1e-3)
-    mufu_fwd = elems * valid * mufu_f / (fwd_ms * 1e-3)
+    issue_peak = 148 * 4 * f_mhz * 1e6  # warp instructions/s: one per SM sub-partition per clock
+    mufu_bwd = valid_elems * mufu_b / (bwd_ms * 1e-3)
+    mufu_fwd = valid_elems * mufu_f / (fwd_ms * 1e-3)
+    counts = _ncu_counts(args.config) if not args.batch else None
     traffic = args.traffic
-    if traffic is None and args.config == "c1" and not args.batch:
-        tf = ROOT / "profiles" / "ncu_traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get("c1", {}).get("ss_bwd_tile_kernel")
+    issue = None
+    if counts:
+        kb, kf = counts["ss_bwd_tile_kernel"], counts["ss_fwd_kernel"]
+        if traffic is None:
+            traffic = round(kb["dram_bytes_per_valid_elem"] * valid_elems)
+        ib = kb["warp_inst_per_valid_elem"] * valid_elems / (bwd_ms * 1e-3)
+        i_f = kf["warp_inst_per_valid_elem"] * valid_elems / (fwd_ms * 1e-3)
+        issue = {"bound": "issue", "unit": "warp inst/s", "peak": issue_peak,
+                 "clock_mhz": f_mhz,
+                 "inst_per_elem": {"fwd": kf["warp_inst_per_valid_elem"],
+                                   "bwd": kb["warp_inst_per_valid_elem"]},
+                 "bwd_frac": round(ib / issue_peak, 4), "fwd_frac": round(i_f / issue_peak, 4),
+                 "source": counts.get("source", "profiles/ncu_counts.json")}
+    fracs = {"bwd": {"hbm": bwd_gbs / hbm, "sfu": mufu_bwd / mufu_peak},
+             "fwd": {"hbm": fwd_gbs / hbm, "sfu": mufu_fwd / mufu_peak}}
+    if issue:
+        fracs["bwd"]["issue"] = issue["bwd_frac"]
+        fracs["fwd"]["issue"] = issue["fwd_frac"]
+    # the binding ceiling of a kernel is the resource it uses the largest share of
+    binding = {k: {"resource": max(v, key=v.get), "frac": round(max(v.values()), 4)}
+               for k, v in fracs.items()}
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "strong" if chan else "weak", "vs_baseline": None,
-        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1)/U(-4,-2) inputs of the config)",
-        "config": {"workload": cfg["workload"], "batch_per_gpu": b, "dim": d_total, "dim_per_gpu": d, "length": L,
-                   "dstate": n, "global_batch": b * world,
-                   "parallelism": (f"channel-sharded over {world} GPUs ({d} channels each)" if chan
-                                   else f"batch-sharded dp{world}") if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (u, delta, z, dy: "
-                         f"{elems * esize * 4 / 1e6:.0f} MB per step)",
-                   "valid_fraction": round(valid, 4)},
+        "higher_is_better": True, "scaling": "strong" if cfg.get("shard") else "weak",
+        "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded N(0,1)/U(-4,-2) inputs of the config)",
+        "value_all_positions": round(value_all, 3),
+        "config": _config_block(cfg, world),
         "kernels_ms": {"fwd": round(fwd_ms, 4), "bwd": round(bwd_ms, 4)},
         "roofline": {"bound": "hbm", "kernel": "ss_bwd_tile_kernel",
                      "achieved": round(bwd_gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -320,9 +473,13 @@ def run_gpu(args, cfg):
                          "bwd_frac": round(mufu_bwd / mufu_peak, 4),
                          "fwd_frac": round(mufu_fwd / mufu_peak, 4),
                          "ops_per_elem": {"fwd": mufu_f, "bwd": mufu_b}},
+        "roofline_issue": issue,
+        "binding": binding,
         "clocks": clocks,
-        "gpu_launches": args.steps * (3 if io == torch.float32 else 5),
+        "gpu_launches": launches,
     }
+    if strong is not None:
+        res["channel_sharded"] = strong
     if e2e is not None:
         res["e2e"] = e2e
     if args.cpu_baseline and world == 1:
@@ -333,7 +490,7 @@ def run_gpu(args, cfg):
     return res
 
 
-def run_e2e(args, cfg, dev, io, rank, world):
+def run_e2e(args, cfg, dev, rank, world):
     """Same metric through the public host-buffer API: pinned host inputs
     copied in and every result copied out, each step, by
     mamba.host_pipeline.HostScanPipeline (copy-in, kernels and copy-out of
@@ -347,6 +504,7 @@ def run_e2e(args, cfg, dev, io, rank, world):
     from mamba.selective_scan_cuda import selective_scan_fn
 
     b, d, L, n = cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"]
+    io = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
     g = torch.Generator()
     g.manual_seed(99 + rank)
 
@@ -358,9 +516,11 @@ def run_e2e(args, cfg, dev, io, rank, world):
     h["A"] = (-torch.arange(1, n + 1, dtype=torch.float32)).expand(d, n).contiguous().pin_memory()
     h["D"] = torch.randn(d, generator=g).pin_memory()
     h["delta_bias"] = (torch.rand(d, generator=g) * 2 - 4).pin_memory()
+    valid_global = b * L * world
     if cfg["padded"]:
-        h["seq_lens"] = torch.randint(512, L + 1, (b,), generator=g,
-                                      dtype=torch.int32).pin_memory()
+        lens, all_lens = _seq_lens(cfg, rank, world)
+        h["seq_lens"] = lens.pin_memory()
+        valid_global = int(all_lens.sum())
     outs = alloc_host_outputs(b, d, L, n, io)
     h2d = sum(t.numel() * t.element_size() for t in h.values())
     d2h = sum(t.numel() * t.element_size() for t in outs.values())
@@ -415,13 +575,14 @@ def run_e2e(args, cfg, dev, io, rank, world):
 
     ms_a, _ = timed(step_autograd)
     ms, k = timed(step)
-    value = b * d * L * world / (ms * 1e-3) / 1e9
+    value = valid_global * d / (ms * 1e-3) / 1e9
     return {"value": round(value, 3), "unit": UNIT, "ms_per_step": round(ms, 3),
             "steps": k, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "api": "mamba.host_pipeline.HostScanPipeline.run (pinned host buffers; "
                    "batch chunks copied in, scanned fwd+bwd and copied out on three streams)",
             "chunk_batch": pipe.chunk,
-            "autograd_value": round(b * d * L * world / (ms_a * 1e-3) / 1e9, 3),
+            "autograd_value": round(valid_global * d / (ms_a * 1e-3) / 1e9, 3),
+            "value_counts": "valid (sequence, channel, step) positions",
             "autograd_api": "selective_scan_fn + autograd backward around whole-batch copies"}
 
 
@@ -668,8 +829,16 @@ def run_block_bench(args):
 
 # ---------------------------------------------------------------- CPU arm
 def _cpu_sample_shape(cfg, seconds_target):
-    # a bounded sample: full length and state size, a slice of the channels
-    return 1, 128 * max(1, os.cpu_count() or 1), cfg["length"], cfg["dstate"]
+    """A bounded sample that is a real slice of the config: one full-length
+    sequence (all steps valid) and its first min(D, 128 x cores) channels."""
+    return 1, min(cfg["dim"], 128 * max(1, os.cpu_count() or 1)), cfg["length"], cfg["dstate"]
+
+
+def _sample_label(cfg, b, d, L, n):
+    return (f"B={b} D={d} L={L} N={n}: one full-length sequence and the first {d} of "
+            f"{cfg['dim']} channels of the config (batch {cfg['batch']}), all steps valid; "
+            "fp32 (NumPy has no bf16); NumPy restatement of the reference math "
+            "(fwd + analytic bwd), JAX absent on this image; throughput per valid position")
 
 
 def _cpu_slice(job):
@@ -709,9 +878,7 @@ def cpu_baseline(cfg, seconds=15.0):
     dt = _cpu_run(cfg, b, d, L, n, threads)
     return {"value": round(b * d * L / dt / 1e9, 6), "unit": UNIT, "cores": threads,
             "kind": "port",
-            "sample": f"B={b} D={d} L={L} N={n} (of B={cfg['batch']} D={cfg['dim']}), fp32, "
-                      f"{dt:.2f} s, NumPy restatement of the reference math "
-                      "(fwd + analytic bwd); JAX absent on this image"}
+            "sample": _sample_label(cfg, b, d, L, n) + f"; {dt:.2f} s"}
 
 
 def run_reference(args, cfg):
@@ -721,21 +888,20 @@ def run_reference(args, cfg):
         return None
     threads = os.cpu_count() or 1
     b, d, L, n = _cpu_sample_shape(cfg, args.cpu_seconds)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     for _ in range(max(0, min(args.warmup, 1))):
         _cpu_run(cfg, b, d, min(L, 256), n, threads)
-    times = [_cpu_run(cfg, b, d, L, n, threads) for _ in range(max(1, min(args.steps, 3)))]
+    times = [_cpu_run(cfg, b, d, L, n, threads) for _ in range(max(1, args.steps))]
     dt = statistics.mean(times)
     value = b * d * L / dt / 1e9
     res = {"metric": METRIC, "value": round(value, 6), "unit": UNIT, "impl": "reference",
-           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(times),
+           "n_gpus": world, "steps": len(times),
            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": cfg["workload"], "batch": cfg["batch"], "dim": cfg["dim"],
-                      "length": cfg["length"], "dstate": cfg["dstate"]},
+           "scaling": "strong" if cfg.get("shard") else "weak", "vs_baseline": None,
+           "dtype": "f32", "data": "synthetic (seeded N(0,1)/U(-4,-2) inputs of the config)",
+           "config": _config_block(cfg, world),
            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads,
-                            "kind": "port",
-                            "sample": f"each step B={b} D={d} L={L} N={n}; NumPy restatement "
-                                      "of the reference's pure-JAX math (JAX not installed)"},
+                            "kind": "port", "sample": "each step " + _sample_label(cfg, b, d, L, n)},
            "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
@@ -750,9 +916,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config",
                     choices=sorted(CONFIGS) + ["step", "conv", "complex", "block", "c3"],
-                    default="c1")
+                    default="c2")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-strong", dest="strong", action="store_false",
+                    help="skip the channel-sharded configs[4] single-sequence leg")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU in place of the config's (small profiling cases)")
@@ -764,7 +932,7 @@ def main():
     if args.config in ("step", "conv", "complex", "block", "c3"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.config} leg has no "
-                              "CPU reference arm; see --config c1"}))
+                              "CPU reference arm; see --config c2"}))
         else:
             {"step": run_step_bench, "conv": run_conv_bench, "complex": run_complex_bench,
              "block": run_block_bench, "c3": run_block_bench}[args.config](args)

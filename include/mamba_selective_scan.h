@@ -56,6 +56,14 @@ const char* mamba_ss_version(void);
  * reference, whose kernels have no waits. */
 uint32_t mamba_ss_take_device_error(void);
 
+/* Number of time segments the launcher cuts each sequence into for this
+ * problem (1 = none; more when there are too few (batch, channel-block) work
+ * units to fill the GPU, or as forced by MAMBA_SS_SEGMENTS). Each segment
+ * count above 1 adds an end-state pass and a combine to the forward and an
+ * adjoint pass and a combine to the backward. No counterpart in the
+ * reference, whose kernels always walk the whole sequence per block. */
+int32_t mamba_ss_segments(int32_t batch, int32_t length, int32_t dim, int32_t dstate);
+
 /* Number of fp32 elements of chunk_states: batch*dim*ceil(length/4)*dstate.
  * The reference sizes the same residual (batch, dim, ceil(L/2048), N, 2)
  * (mamba/selective_scan_cuda.py:129-134); it is private to the custom_vjp. */

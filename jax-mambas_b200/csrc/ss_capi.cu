@@ -140,6 +140,11 @@ uint32_t mamba_ss_take_device_error(void) {
   return mss::take_fwd_device_error() | mss::take_bwd_device_error();
 }
 
+int32_t mamba_ss_segments(int32_t batch, int32_t length, int32_t dim, int32_t dstate) {
+  if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
+  return mss::seg_plan(batch, length, dim, dstate).n_seg;
+}
+
 int64_t mamba_ss_chunk_states_elems(int32_t batch, int32_t length, int32_t dim,
                                     int32_t dstate) {
   if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;

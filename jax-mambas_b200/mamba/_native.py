@@ -95,6 +95,7 @@ SIGNATURES = {
         + [_c_void_p] * 16  # initial_state seq_lens chunk_states out_pre dout dlast du ddelta dA dB dC dD dz dbias dinit workspace
         + [ctypes.c_size_t],
     ),
+    "mamba_ss_segments": (_i32, [_i32, _i32, _i32, _i32]),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,

@@ -36,12 +36,34 @@ def channel_shard(dim: int, rank: int, world: int) -> slice:
     return batch_shard(dim, rank, world)
 
 
-def allreduce_bc_grads(dB: torch.Tensor, dC: torch.Tensor, group=None):
-    """Sum dB and dC over the channel shards, in place (one all-reduce each)."""
+def token_balanced_shards(lengths, world: int):
+    """Assign sequences to ranks, the same count each, balancing valid tokens.
+
+    Right-padded batches cost each rank its valid steps, and every step waits
+    for the slowest rank, so a data loader deals sequences out by length:
+    sorted longest first, then dealt in a snake order (0, 1, .., w-1, w-1, ..,
+    0, 0, 1, ..), which bounds any two ranks' token counts to within one
+    sequence's length of each other. Returns one list of sequence indices per
+    rank; ``len(lengths)`` must be a multiple of ``world``."""
+    n = len(lengths)
+    if world <= 0 or n % world:
+        raise ValueError(f"{n} sequences do not split evenly over {world} ranks")
+    order = sorted(range(n), key=lambda i: (-int(lengths[i]), i))
+    shards = [[] for _ in range(world)]
+    for k, i in enumerate(order):
+        r, lap = k % world, k // world
+        shards[r if lap % 2 == 0 else world - 1 - r].append(i)
+    return shards
+
+
+def allreduce_bc_grads(dB: torch.Tensor, dC: torch.Tensor, group=None, async_op=False):
+    """Sum dB and dC over the channel shards, in place (one all-reduce each).
+    With ``async_op`` the two work handles are returned (wait() on each makes
+    the current stream wait for it)."""
     if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
-        return
-    dist.all_reduce(dB, op=dist.ReduceOp.SUM, group=group)
-    dist.all_reduce(dC, op=dist.ReduceOp.SUM, group=group)
+        return []
+    return [dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+            for t in (dB, dC)]
 
 
 def flat_param_grads(dim: int, dstate: int, device=None, dtype=torch.float32):

@@ -123,3 +123,18 @@ def test_two_rank_channel_sharding_matches_full_sequence():
         sl = channel_shard(10, r, 2)
         np.testing.assert_allclose(dA, full["dA"][sl], rtol=1e-12, atol=1e-12)
         np.testing.assert_allclose(du, full["du"][:, sl], rtol=1e-12, atol=1e-12)
+
+
+def test_token_balanced_shards():
+    from mamba.distributed import token_balanced_shards
+
+    rng = np.random.default_rng(0)
+    for world in (1, 2, 4, 8):
+        lens = rng.integers(512, 4097, 16 * world)
+        shards = token_balanced_shards(lens, world)
+        assert sorted(i for s in shards for i in s) == list(range(16 * world))
+        assert all(len(s) == 16 for s in shards)
+        sums = [int(lens[s].sum()) for s in shards]
+        assert max(sums) - min(sums) <= lens.max()
+    with pytest.raises(ValueError):
+        token_balanced_shards([1, 2, 3], 2)
