@@ -56,6 +56,16 @@ const char* mamba_ss_version(void);
  * reference, whose kernels have no waits. */
 uint32_t mamba_ss_take_device_error(void);
 
+/* Test hook for the bounded waits: sets the number of polls after which
+ * the scan kernels launched from now on (any host thread) give up waiting
+ * for a tile's TMA staging, report bit 0 through
+ * mamba_ss_take_device_error() and return with incomplete outputs (they
+ * still let their copies in flight land first). 0 makes every such wait
+ * give up at once; a negative value restores the default (2^22 polls, far
+ * longer than any copy takes). No counterpart in the reference, whose
+ * kernels do not wait on copies. */
+void mamba_ss_debug_set_wait_polls(int64_t polls);
+
 /* Number of time segments the launcher cuts each sequence into for this
  * problem (1 = none; more when there are too few (batch, channel-block) work
  * units to fill the GPU, or as forced by MAMBA_SS_SEGMENTS). Each segment

@@ -75,8 +75,10 @@ struct TileShared {
   alignas(1024) T rawU[2][kCh][kBT];  // u in, du out
   alignas(1024) T rawY[2][kCh][kBT];  // dout in; (fp32: dy)
   alignas(1024) T rawZ[2][kCh][kBT];  // z in, dz out
-  alignas(1024) T rawB[2][kNSP][kBT];
-  alignas(1024) T rawC[2][kNSP][kBT];
+  // B and C staged as fp32 whatever the I/O type (bf16 I/O: from the
+  // launcher's widened copies), read in place through the 128-byte swizzle
+  alignas(1024) float rawB[2][kNSP][kBT];
+  alignas(1024) float rawC[2][kNSP][kBT];
   alignas(1024) T rawP[kCh][kBT];     // pre-gate output (read by the transform only)
   // bf16 I/O: fp32 work rows delta_eff and dy, swizzled like fp32 staging
   alignas(16) float wD[kInPlace ? 1 : kCh][kBT];
@@ -254,7 +256,7 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
   // to buffer i & 1 (bar[i & 1]), its pre-gate rows to the single rawP (barP,
   // issued once the previous position's transform has read rawP).
   constexpr uint32_t kChBytes = kCh * kBT * sizeof(T);
-  constexpr uint32_t kNBytes = NS * kBT * sizeof(T);
+  constexpr uint32_t kNBytes = NS * kBT * sizeof(float);
   const int rc = static_cast<int>(row0);
   auto issue = [&](int i) {  // one thread
     const int s = i & 1;
@@ -313,8 +315,8 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     T* bU = &sh.rawU[s][0][0];
     T* bY = &sh.rawY[s][0][0];
     T* bZ = &sh.rawZ[s][0][0];
-    const T* bB = &sh.rawB[s][0][0];
-    const T* bC = &sh.rawC[s][0][0];
+    const float* bB = &sh.rawB[s][0][0];
+    const float* bC = &sh.rawC[s][0][0];
     // fp32 work rows: delta_eff and dy
     float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
     float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
@@ -360,8 +362,8 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     float* const acc_row = (((c & 1) != 0 ? dC_b : dB_b) + static_cast<size_t>(st_of(0)) * L) + t0;
 
     if (use_tma) {
-      bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
-      if (has_z) ok = ok && mbar_wait_bounded(&sh.barP, i & 1);
+      bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1, p.wait_polls);
+      if (has_z) ok = ok && mbar_wait_bounded(&sh.barP, i & 1, p.wait_polls);
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) {
           atomicOr(&g_bwd_device_error, kErrTmaTimeout);
@@ -383,8 +385,8 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
                          t0, lane);
       }
       const size_t brow = static_cast<size_t>(b) * NS;
-      stage_tile_plain(&sh.rawB[s][0][0], static_cast<const T*>(p.B), brow, NS, NS, L, t0, lane);
-      stage_tile_plain(&sh.rawC[s][0][0], static_cast<const T*>(p.C), brow, NS, NS, L, t0, lane);
+      stage_tile_plain(&sh.rawB[s][0][0], p.B32, brow, NS, NS, L, t0, lane);
+      stage_tile_plain(&sh.rawC[s][0][0], p.C32, brow, NS, NS, L, t0, lane);
       __syncwarp();
     }
 
@@ -449,7 +451,7 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     T* const rU = bU + c * kBT;
     T* const rDo = bD + c * kBT;  // ddelta out (in place of delta)
     const int kW = row_key(wD, c), kU = row_key(bU, c);
-    const T* rB[kS];
+    const float* rB[kS];
     int kB[kS];
 #pragma unroll
     for (int j = 0; j < kS; ++j) {
@@ -457,7 +459,7 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
       kB[j] = row_key(bB, st_of(j));
     }
     constexpr int kCfromB = Sh::kNSP * 2 * kBT;  // rawC[s] - rawB[s], elements
-    static_assert(offsetof(Sh, rawC) - offsetof(Sh, rawB) == kCfromB * sizeof(T), "B/C");
+    static_assert(offsetof(Sh, rawC) - offsetof(Sh, rawB) == kCfromB * sizeof(float), "B/C");
 
     // delta_eff and delta_eff u (ZOH: u) of group g; delta_eff is zero past
     // the end, so delta_eff u is too (ZOH: b_bar = expm1(0) / A = 0)
@@ -737,7 +739,7 @@ __global__ void __launch_bounds__(32)
   const float bias = p.delta_bias ? __ldg(p.delta_bias + d) : 0.f;
 
   constexpr uint32_t kChBytes = kCh * kBT * sizeof(T);
-  constexpr uint32_t kNBytes = NS * kBT * sizeof(T);
+  constexpr uint32_t kNBytes = NS * kBT * sizeof(float);
   const int rc = static_cast<int>(row0);
   auto issue = [&](int i) {  // one thread: position i = tile k_last - i
     const int s = i & 1;
@@ -769,7 +771,7 @@ __global__ void __launch_bounds__(32)
     T* bD = &sh.rawD[s][0][0];
     T* bY = &sh.rawY[s][0][0];
     T* bZ = &sh.rawZ[s][0][0];
-    const T* bC = &sh.rawC[s][0][0];
+    const float* bC = &sh.rawC[s][0][0];
     float* wD = Sh::kInPlace ? reinterpret_cast<float*>(bD) : &sh.wD[0][0];
     float* wY = Sh::kInPlace ? reinterpret_cast<float*>(bY) : &sh.wY[0][0];
     if (use_tma) {
@@ -777,7 +779,7 @@ __global__ void __launch_bounds__(32)
         fence_proxy_async_smem();  // the warp is done with the other buffer
         issue(i + 1);
       }
-      const bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
+      const bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1, p.wait_polls);
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) {
           atomicOr(&g_bwd_device_error, kErrTmaTimeout);
@@ -791,7 +793,7 @@ __global__ void __launch_bounds__(32)
       stage_tile_plain(bY, static_cast<const T*>(p.dout), row0, n_ch, kCh, L, t0, lane);
       if (has_z)
         stage_tile_plain(bZ, static_cast<const T*>(p.z), row0, n_ch, kCh, L, t0, lane);
-      stage_tile_plain(&sh.rawC[s][0][0], static_cast<const T*>(p.C),
+      stage_tile_plain(&sh.rawC[s][0][0], static_cast<const float*>(p.C32),
                            static_cast<size_t>(b) * NS, NS, NS, L, t0, lane);
       __syncwarp();
     }
@@ -829,7 +831,7 @@ __global__ void __launch_bounds__(32)
     const float* rD = wD + c * kBT;
     const float* rY = wY + c * kBT;
     const int kW = row_key(wD, c);
-    const T* rC[kS];
+    const float* rC[kS];
     int kC[kS];
 #pragma unroll
     for (int j = 0; j < kS; ++j) {
@@ -931,6 +933,19 @@ cudaError_t launch_param_reduce(const float* dA_part, const float* dD_part,
   return cudaPeekAtLastError();
 }
 
+// B and C widened to fp32 for the scan kernels (bf16 I/O): blockIdx.y picks
+// the array; exact (a bf16 is the upper half of an fp32).
+__global__ void bf16_to_f32_pair_kernel(const __nv_bfloat16* __restrict__ B,
+                                        const __nv_bfloat16* __restrict__ C,
+                                        float* __restrict__ B32, float* __restrict__ C32,
+                                        size_t n) {
+  const __nv_bfloat16* src = blockIdx.y == 0 ? B : C;
+  float* dst = blockIdx.y == 0 ? B32 : C32;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = __bfloat162float(src[i]);
+}
+
 __global__ void f32_to_bf16_kernel(const float* __restrict__ src,
                                    __nv_bfloat16* __restrict__ dst, size_t n) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
@@ -1030,7 +1045,7 @@ static cudaError_t launch_bwd_tile(const BwdParams& p, int dstate, int io_dtype,
   memset(&maps, 0, sizeof(maps));
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
   const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  pk.tma_ok = (p.seqlen * esize) % 16 == 0 && al16(p.B) && al16(p.C) && al16(p.u) &&
+  pk.tma_ok = (p.seqlen * esize) % 16 == 0 && al16(p.B32) && al16(p.C32) && al16(p.u) &&
               al16(p.delta) && al16(p.dout) && al16(p.du) && al16(p.ddelta) &&
               (!p.z || (al16(p.z) && al16(p.dz) && al16(p.out_pre)));
   if (pk.tma_ok) {
@@ -1039,8 +1054,8 @@ static cudaError_t launch_bwd_tile(const BwdParams& p, int dstate, int io_dtype,
     const uint64_t L = p.seqlen;
     const uint32_t ch = static_cast<uint32_t>(tile_channels(dstate));
     const uint32_t ns = static_cast<uint32_t>(dstate);
-    pk.tma_ok = encode_tile(&maps.b, p.B, io_dtype, brows, L, ns) &&
-                encode_tile(&maps.c, p.C, io_dtype, brows, L, ns) &&
+    pk.tma_ok = encode_tile(&maps.b, p.B32, MSS_F32, brows, L, ns) &&
+                encode_tile(&maps.c, p.C32, MSS_F32, brows, L, ns) &&
                 encode_tile(&maps.u, p.u, io_dtype, rows, L, ch) &&
                 encode_tile(&maps.d, p.delta, io_dtype, rows, L, ch) &&
                 encode_tile(&maps.y, p.dout, io_dtype, rows, L, ch) &&
@@ -1066,6 +1081,16 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
   e = cudaMemsetAsync(p.dC_acc, 0, n_bnl * sizeof(float), stream);
   if (e != cudaSuccess) return e;
 
+  if (io_dtype == MSS_BF16) {
+    const int threads = 256;
+    const unsigned blocks = static_cast<unsigned>(
+        std::min<size_t>((n_bnl + threads - 1) / threads, 148 * 8));
+    bf16_to_f32_pair_kernel<<<dim3(blocks, 2), threads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(p.B), static_cast<const __nv_bfloat16*>(p.C), p.B32,
+        p.C32, n_bnl);
+    e = cudaPeekAtLastError();
+    if (e != cudaSuccess) return e;
+  }
   e = launch_bwd_tile(p, dstate, io_dtype, zoh, stream);
   if (e != cudaSuccess) return e;
   return launch_bwd_finish(p, dstate, io_dtype, dB_out, dC_out, dA, dD, ddelta_bias, stream);

@@ -4,6 +4,7 @@
 // native/selective_scan_bwd.cu:45-79), launch on the caller's stream and
 // report errors through a status code plus a per-thread message.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <cstdlib>
@@ -14,6 +15,10 @@
 namespace {
 
 thread_local std::string g_last_error;
+
+// poll limit of the scan kernels' staging waits (test hook; see
+// mamba_ss_debug_set_wait_polls)
+std::atomic<uint32_t> g_wait_polls{mss::kWaitPolls};
 
 mss_status fail(mss_status code, const std::string& msg) {
   g_last_error = msg;
@@ -54,7 +59,8 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 struct BwdWorkspace {
   int n_seg, seg_tiles;
-  size_t dA_part, dD_part, dbias_part, seg_G, seg_dsum, seg_carry, dB_acc, dC_acc, total;
+  size_t dA_part, dD_part, dbias_part, seg_G, seg_dsum, seg_carry, dB_acc, dC_acc, B32, C32,
+      total;
 };
 
 BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
@@ -81,13 +87,18 @@ BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
     w.seg_carry = off;
     off += align256(sizeof(float) * sbd * dstate);
   }
-  w.dB_acc = w.dC_acc = 0;
+  w.dB_acc = w.dC_acc = w.B32 = w.C32 = 0;
   if (io_dtype == MSS_BF16) {
+    // fp32 accumulators of dB / dC, and B / C widened to fp32 for the kernels
     const size_t bnl =
         align256(sizeof(float) * static_cast<size_t>(batch) * dstate * length);
     w.dB_acc = off;
     off += bnl;
     w.dC_acc = off;
+    off += bnl;
+    w.B32 = off;
+    off += bnl;
+    w.C32 = off;
     off += bnl;
   }
   w.total = off;
@@ -140,6 +151,12 @@ uint32_t mamba_ss_take_device_error(void) {
   return mss::take_fwd_device_error() | mss::take_bwd_device_error();
 }
 
+void mamba_ss_debug_set_wait_polls(int64_t polls) {
+  g_wait_polls.store(polls < 0 ? mss::kWaitPolls
+                               : static_cast<uint32_t>(std::min<int64_t>(polls, mss::kWaitPolls)),
+                     std::memory_order_relaxed);
+}
+
 int32_t mamba_ss_segments(int32_t batch, int32_t length, int32_t dim, int32_t dstate) {
   if (batch <= 0 || length <= 0 || dim <= 0 || dstate <= 0) return 0;
   return mss::seg_plan(batch, length, dim, dstate).n_seg;
@@ -174,6 +191,7 @@ mss_status mamba_ss_fused_fwd(
   if (reinterpret_cast<uintptr_t>(chunk_states) & 15)
     return fail(MSS_INVALID_ARGUMENT, "mamba_ss_fused_fwd: chunk_states must be 16-byte aligned");
   mss::FwdParams p{};
+  p.wait_polls = g_wait_polls.load(std::memory_order_relaxed);
   p.batch = batch;
   p.dim = dim;
   p.seqlen = length;
@@ -232,6 +250,7 @@ mss_status mamba_ss_fused_bwd(
                 "mamba_ss_fused_bwd: workspace must be 256-byte aligned");
   char* ws = static_cast<char*>(workspace);
   mss::BwdParams p{};
+  p.wait_polls = g_wait_polls.load(std::memory_order_relaxed);
   p.batch = batch;
   p.dim = dim;
   p.seqlen = length;
@@ -267,9 +286,13 @@ mss_status mamba_ss_fused_bwd(
   if (io_dtype == MSS_BF16) {
     p.dB_acc = reinterpret_cast<float*>(ws + w.dB_acc);
     p.dC_acc = reinterpret_cast<float*>(ws + w.dC_acc);
+    p.B32 = reinterpret_cast<float*>(ws + w.B32);
+    p.C32 = reinterpret_cast<float*>(ws + w.C32);
   } else {
     p.dB_acc = static_cast<float*>(dB);
     p.dC_acc = static_cast<float*>(dC);
+    p.B32 = static_cast<float*>(const_cast<void*>(B));
+    p.C32 = static_cast<float*>(const_cast<void*>(C));
   }
   p.dh0 = dinitial_state;
   cudaError_t e = mss::launch_bwd(p, dstate, io_dtype, discretization, dB, dC,

@@ -70,6 +70,7 @@ struct FwdParams {
   int batch, dim, seqlen, n_chunks;  // n_chunks: saved carries per row, ceil(L / kCkpt)
   int delta_softplus;
   int tma_ok;  // rows may be staged with TMA bulk copies (set by the launcher)
+  unsigned int wait_polls;  // poll limit of the staging waits (set by the launcher)
   const void* u;
   const void* delta;
   const void* z;
@@ -98,6 +99,7 @@ struct BwdParams {
   int batch, dim, seqlen, n_chunks;
   int delta_softplus;
   int tma_ok;  // B/C may be staged with TMA (set by the launcher)
+  unsigned int wait_polls;  // poll limit of the staging waits (set by the launcher)
   const void* u;
   const void* delta;
   const void* z;
@@ -115,6 +117,10 @@ struct BwdParams {
   void* du;
   void* ddelta;
   void* dz;
+  // B and C as fp32 (batch, dstate, L), what the scan kernels read: the
+  // inputs themselves for fp32 I/O, a copy widened by the launcher for bf16
+  float* B32;
+  float* C32;
   float* dB_acc;   // fp32 (batch, dstate, L), zeroed before the launch
   float* dC_acc;
   float* dA_part;  // fp32 (n_seg, batch, dim, dstate): per-batch partial sums
@@ -357,9 +363,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for phase `parity` of `bar` to complete, giving up after a bounded
 // number of polls (each try_wait suspends the thread for a short,
 // hardware-defined time). Returns false on timeout.
+// `polls` bounds the wait of a tile's staging (the launcher passes
+// kWaitPolls unless mamba_ss_debug_set_wait_polls() lowered it); the waits
+// that drain copies in flight before an early exit always use kWaitPolls.
 constexpr uint32_t kWaitPolls = 1u << 22;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitPolls; ++i)
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint32_t polls = kWaitPolls) {
+  for (uint32_t i = 0; i < polls; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }

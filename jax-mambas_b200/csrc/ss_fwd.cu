@@ -234,15 +234,17 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     const int s = kk & 1;
     const int t0 = k * kTile;
     if (use_tma) {
-      const bool ok = mbar_wait_bounded(&sh.bar[s], (kk >> 1) & 1);
+      const bool ok = mbar_wait_bounded(&sh.bar[s], (kk >> 1) & 1, p.wait_polls);
       // the CTA's one barrier per tile (TMA staging): past it every warp is
       // done with the previous tile, whose staging buffer the next copies fill
       if (__syncthreads_or(!ok)) {
-        // A copy never completed: report it, let the in-flight copies of the
-        // other buffer finish (bounded), and leave.
+        // A copy did not complete in time: report it, let the copy in
+        // flight into this CTA's staging land (bounded), and leave. Tile k's
+        // copies are the only ones in flight: the next tile's are issued
+        // only after this wait succeeds.
         if (tid == 0) {
           atomicOr(&g_fwd_device_error, kErrTmaTimeout);
-          if (k + 1 < k_end) mbar_wait_bounded(&sh.bar[s ^ 1], ((kk + 1) >> 1) & 1);
+          mbar_wait_bounded(&sh.bar[s], (kk >> 1) & 1);
         }
         return;
       }
