@@ -84,7 +84,14 @@ class ClockSampler:
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
-        time.sleep(0.3)
+        # start timing only once the sampler is writing (nvidia-smi can take
+        # a second or more to come up, longer than a short timed region)
+        t_end = time.time() + 5.0
+        while self.proc is not None and time.time() < t_end:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.05)
+        time.sleep(0.1)
         return self
 
     def __exit__(self, *exc):

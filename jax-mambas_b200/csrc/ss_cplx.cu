@@ -72,6 +72,40 @@ __device__ __forceinline__ float2 cis(float x) {
   return make_float2(c, sn);
 }
 
+// cis() for two arguments at once: the same reduction and series with
+// packed fp32x2 arithmetic (the quadrant logic per component). Returns
+// (cos x.x, cos x.y) in c and (sin x.x, sin x.y) in s.
+__device__ __forceinline__ void cis2(float2 x, float2& c, float2& s) {
+  constexpr float kTwoOverPi = 0x1.45f306p-1f;
+  constexpr float kP1 = 0x1.921fb6p+0f, kP2 = -0x1.777a5cp-25f, kP3 = -0x1.ee59dap-50f;
+  const float2 q = mul2(x, dup2(kTwoOverPi));
+  const float2 kf = make_float2(rintf(q.x), rintf(q.y));
+  const float2 nkf = make_float2(-kf.x, -kf.y);
+  float2 r = fma2(nkf, dup2(kP1), x);
+  r = fma2(nkf, dup2(kP2), r);
+  r = fma2(nkf, dup2(kP3), r);
+  const int k0 = static_cast<int>(kf.x), k1 = static_cast<int>(kf.y);
+  const float2 r2 = mul2(r, r);
+  float2 ps = fma2(r2, dup2(1.f / 362880.f), dup2(-1.f / 5040.f));
+  ps = fma2(ps, r2, dup2(1.f / 120.f));
+  ps = fma2(ps, r2, dup2(-1.f / 6.f));
+  const float2 sr = fma2(mul2(ps, r2), r, r);
+  float2 pc = fma2(r2, dup2(-1.f / 3628800.f), dup2(1.f / 40320.f));
+  pc = fma2(pc, r2, dup2(-1.f / 720.f));
+  pc = fma2(pc, r2, dup2(1.f / 24.f));
+  pc = fma2(pc, r2, dup2(-0.5f));
+  const float2 cr = fma2(pc, r2, dup2(1.f));
+  auto quad = [](int k, float cv, float sv, float& co, float& so) {
+    const bool swap = (k & 1) != 0;
+    co = swap ? sv : cv;
+    so = swap ? cv : sv;
+    if (((k + 1) & 2) != 0) co = -co;
+    if ((k & 2) != 0) so = -so;
+  };
+  quad(k0, cr.x, sr.x, c.x, s.x);
+  quad(k1, cr.y, sr.y, c.y, s.y);
+}
+
 struct Cx {
   float r, i;
 };
@@ -81,6 +115,19 @@ __device__ __forceinline__ Cx cmulc(Cx a, Cx b) {  // a * conj(b)
 }
 __device__ __forceinline__ Cx cconj(Cx a) { return {a.r, -a.i}; }
 __device__ __forceinline__ Cx cld(const float2* p) { const float2 v = *p; return {v.x, v.y}; }
+
+// Euler discretization of two states at one step: a_j = exp(delta A_j) =
+// 2^(delta Re A_j log2 e) cis(delta Im A_j), the modulus from the SFU's ex2
+// (as the real kernels' decay), the rotation from cis2.
+__device__ __forceinline__ void cdisc_euler2(float dl, Cx A0, Cx A1, Cx& a0, Cx& a1) {
+  float2 c, sn;
+  cis2(mul2(dup2(dl), make_float2(A0.i, A1.i)), c, sn);
+  const float2 arg = mul2(dup2(dl * kLog2e), make_float2(A0.r, A1.r));
+  const float m0 = ex2(arg.x), m1 = ex2(arg.y);
+  const float2 re = mul2(make_float2(m0, m1), c), im = mul2(make_float2(m0, m1), sn);
+  a0 = {re.x, im.x};
+  a1 = {re.y, im.y};
+}
 
 // a = exp(delta A) and (ZOH) bb = expm1(delta A) / A, for complex A = (ar, ai)
 template <bool kZOH>
@@ -169,11 +216,20 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
       const float uv = sh.uu[cl][tt];
       const float dlu = dl * uv;
       float yp = 0.f;
+      Cx av[kS], bbs[kS];
+#pragma unroll
+      for (int j = 0; j < kS; ++j) {
+        if (!kZOH && (j & 1) == 0 && j + 1 < kS) {
+          cdisc_euler2(dl, Av[j], Av[j + 1], av[j], av[j + 1]);
+          bbs[j] = bbs[j + 1] = {dl, 0.f};
+        } else if (kZOH || (j & 1) == 0) {
+          cdisc<kZOH>(dl, Av[j], av[j], bbs[j]);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < kS; ++j) {
         const int n = q + kLPC * j;
-        Cx a, bb;
-        cdisc<kZOH>(dl, Av[j], a, bb);
+        const Cx a = av[j], bb = bbs[j];
         const Cx Bn = cld(&sh.Bt[n][tt]);
         // Euler: b_bar u = delta u B (real times complex)
         const Cx bu = kZOH ? cmul(bb, {Bn.r * uv, Bn.i * uv}) : Cx{dlu * Bn.r, dlu * Bn.i};
@@ -328,8 +384,16 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads =
         const float dlu = dl * uv;
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
+          if (!kZOH && (j & 1) == 0 && j + 1 < kS) {
+            cdisc_euler2(dl, Av[j], Av[j + 1], aa[e][j], aa[e][j + 1]);
+            bbv[e][j] = bbv[e][j + 1] = {dl, 0.f};
+          } else if (kZOH || (j & 1) == 0) {
+            cdisc<kZOH>(dl, Av[j], aa[e][j], bbv[e][j]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kS; ++j) {
           const int n = q + kLPC * j;
-          cdisc<kZOH>(dl, Av[j], aa[e][j], bbv[e][j]);
           const Cx Bn = cld(&sh.Bt[n][tg + e]);
           const Cx bu =
               kZOH ? cmul(bbv[e][j], {Bn.r * uv, Bn.i * uv}) : Cx{dlu * Bn.r, dlu * Bn.i};
