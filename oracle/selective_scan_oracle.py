@@ -24,11 +24,20 @@ It restates, in NumPy, the math of the JAX-Mambas reference:
   ``cache ++ projed``, silu, mask) and its adjoint; the CPU tests pin them
   against torch's grouped conv1d under autograd in float64.
 
-Parity pinning: the reference ships no golden vectors and cannot run here
-(JAX is not installed on this image or on the GPU box). The oracle is pinned
-by restating the reference's own known-answer test (associative scan vs
-sequential recurrence, ``tests/test_selective_scan_cuda.py:22-52``) and by
-autograd cross-checks of the backward; see ``tests/test_oracle.py``.
+Parity pinning: the reference ships no golden vectors and JAX is not
+installed on this image or on the GPU box, so the reference's own functions
+were executed here instead: tests/golden/make_ref_golden.py lifts
+``selective_scan_reference`` (``mamba/selective_scan_cuda.py:56-90``) and
+``S6.discretize`` / ``S6.binary_operator`` (``mamba/mamba1.py:143-158``) out
+of the reference source unmodified and runs them in float64 under a
+torch-backed stand-in for ``jax.numpy`` / ``lax.associative_scan``, with
+torch.autograd for the vector-Jacobian products. tests/test_ref_golden.py
+checks this oracle against those fixtures (tests/golden/ref_*.npz) to 1e-6:
+the reference test recipe at six lengths and both discretizations, configs[0]
+with the fused layer math, mask-style padding and the complex branch. The
+restated known-answer test (associative scan vs sequential recurrence,
+``tests/test_selective_scan_cuda.py:22-52``) and autograd cross-checks of the
+analytic backward stay in ``tests/test_oracle.py``.
 """
 from __future__ import annotations
 
