@@ -66,10 +66,15 @@ struct TileMaps {
   CUtensorMap du, dd, dz;           // stores
 };
 
-template <int NS, typename T>
+// kW warps per CTA (N = 16 only: 2): the warps share the staging of B and
+// C and every TMA copy covers all kCh channels of the CTA; with more than one
+// warp the pre-gate rows are double-buffered with the other arrays, so that
+// the CTA needs one barrier per tile.
+template <int NS, typename T, int kW = 1>
 struct TileShared {
-  static constexpr int kCh = TileCfg<NS>::kCh;
+  static constexpr int kCh = TileCfg<NS>::kCh * kW;
   static constexpr int kNSP = NS < 8 ? 8 : NS;  // whole swizzle atoms
+  static constexpr int kPB = kW > 1 ? 2 : 1;    // pre-gate buffers
   static constexpr bool kInPlace = sizeof(T) == 4;  // fp32 work rows live in rawD / rawY
   alignas(1024) T rawD[2][kCh][kBT];  // delta in; (fp32: delta_eff;) ddelta out
   alignas(1024) T rawU[2][kCh][kBT];  // u in, du out
@@ -79,7 +84,7 @@ struct TileShared {
   // launcher's widened copies), read in place through the 128-byte swizzle
   alignas(1024) float rawB[2][kNSP][kBT];
   alignas(1024) float rawC[2][kNSP][kBT];
-  alignas(1024) T rawP[kCh][kBT];     // pre-gate output (read by the transform only)
+  alignas(1024) T rawP[kPB][kCh][kBT];  // pre-gate output (read by the transform only)
   // bf16 I/O: fp32 work rows delta_eff and dy, swizzled like fp32 staging
   alignas(16) float wD[kInPlace ? 1 : kCh][kBT];
   alignas(16) float wY[kInPlace ? 1 : kCh][kBT];
@@ -188,25 +193,34 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, 
 // (batch_of_row); its bound of 16 CTAs per SM keeps the registers at the plain
 // kernel's 128 (the ranking code otherwise lifts them to ~170, which cuts the
 // resident warps per SM from 16 to 12). 0 leaves the bound to the compiler.
-template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false>
-__global__ void __launch_bounds__(32, kLPT ? 16 : 0)
+// kWarps: warps per CTA (TileShared); the CTA's kCh channels are kWarps
+// blocks of kCPW, one per warp.
+template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false, int kWarps = 1>
+__global__ void __launch_bounds__(32 * kWarps, kLPT ? 16 / kWarps : 0)
     ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
   using Cfg = TileCfg<NS>;
-  using Sh = TileShared<NS, T>;
+  using Sh = TileShared<NS, T, kWarps>;
   constexpr int kS = Cfg::kS;
   constexpr int kLPC = Cfg::kLPC;
-  constexpr int kCh = Cfg::kCh;
+  constexpr int kCPW = Cfg::kCh;  // channels per warp
+  constexpr int kCh = Sh::kCh;    // channels per CTA
+  static_assert(kWarps == 1 || NS == 16, "multi-warp CTAs are for N = 16");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
 
-  const int lane = threadIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int b = kLPT ? batch_of_row(p.seq_lens, p.batch, p.seqlen, static_cast<int>(blockIdx.y))
                      : static_cast<int>(blockIdx.y);
   const int d0 = blockIdx.x * kCh;
   const int L = p.seqlen;
   const int n_ch = min(kCh, p.dim - d0);
-  const int c = lane / kLPC;  // channel slot
+  const int c = warp * kCPW + lane / kLPC;  // channel slot in the CTA
   const int q = lane % kLPC;  // lane q owns states q, q + kLPC, ...
+  // this warp's block of channel rows: [wc0, wc0 + n_wch)
+  const int wc0 = warp * kCPW;
+  const int n_wch = max(0, min(kCPW, n_ch - wc0));
   const bool act = c < n_ch;
   const int d = d0 + (act ? c : 0);
   const size_t row = static_cast<size_t>(b) * p.dim + d;
@@ -247,14 +261,18 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     const int tz = max(k_last + 1, k_begin) * kBT;
     const int te = min(k_end * kBT, L);
     const bool vec = use_tma;  // 16-byte aligned rows (L * esize % 16 == 0)
-    zero_rows(static_cast<T*>(p.du), row0, n_ch, L, tz, te, vec, lane);
-    zero_rows(static_cast<T*>(p.ddelta), row0, n_ch, L, tz, te, vec, lane);
-    if (has_z) zero_rows(static_cast<T*>(p.dz), row0, n_ch, L, tz, te, vec, lane);
+    zero_rows(static_cast<T*>(p.du), row0 + wc0, n_wch, L, tz, te, vec, lane);
+    zero_rows(static_cast<T*>(p.ddelta), row0 + wc0, n_wch, L, tz, te, vec, lane);
+    if (has_z) zero_rows(static_cast<T*>(p.dz), row0 + wc0, n_wch, L, tz, te, vec, lane);
   }
 
   // TMA pipeline: position i of the walk is tile k_last - i; its arrays go
-  // to buffer i & 1 (bar[i & 1]), its pre-gate rows to the single rawP (barP,
-  // issued once the previous position's transform has read rawP).
+  // to buffer i & 1 (bar[i & 1]). One warp: its pre-gate rows go to the
+  // single rawP (barP, issued once the previous position's transform has
+  // read rawP). Several warps: the pre-gate rows travel with the other
+  // arrays in buffer i & 1, and the CTA meets one barrier per tile, after the
+  // transform: past it every warp is done with position i - 1, whose rows
+  // thread 0 then stores and whose buffer it refills with position i + 1.
   constexpr uint32_t kChBytes = kCh * kBT * sizeof(T);
   constexpr uint32_t kNBytes = NS * kBT * sizeof(float);
   const int rc = static_cast<int>(row0);
@@ -262,30 +280,45 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     const int s = i & 1;
     const int x = (k_last - i) * kBT;
     uint64_t* bar = &sh.bar[s];
-    mbar_arrive_expect_tx(bar, (has_z ? 4u : 3u) * kChBytes + 2u * kNBytes);
+    const uint32_t n_ch_arrays = (has_z ? 4u : 3u) + (kWarps > 1 && has_z ? 1u : 0u);
+    mbar_arrive_expect_tx(bar, n_ch_arrays * kChBytes + 2u * kNBytes);
     tma_load_2d(&sh.rawD[s][0][0], &maps.d, x, rc, bar);
     tma_load_2d(&sh.rawU[s][0][0], &maps.u, x, rc, bar);
     tma_load_2d(&sh.rawY[s][0][0], &maps.y, x, rc, bar);
     if (has_z) tma_load_2d(&sh.rawZ[s][0][0], &maps.z, x, rc, bar);
+    if (kWarps > 1 && has_z) tma_load_2d(&sh.rawP[s % Sh::kPB][0][0], &maps.p, x, rc, bar);
     tma_load_2d(&sh.rawB[s][0][0], &maps.b, x, b * NS, bar);
     tma_load_2d(&sh.rawC[s][0][0], &maps.c, x, b * NS, bar);
   };
-  auto issue_pre = [&](int i) {  // one thread
+  auto issue_pre = [&](int i) {  // one thread (one-warp CTAs)
     mbar_arrive_expect_tx(&sh.barP, kChBytes);
     tma_load_2d(&sh.rawP[0][0], &maps.p, (k_last - i) * kBT, rc, &sh.barP);
   };
-  if (use_tma && lane == 0) {
+  // the du / ddelta / dz rows of position i (multi-warp CTAs, thread 0)
+  auto store_pos = [&](int i) {
+    const int s = i & 1;
+    const int x = (k_last - i) * kBT;
+    tma_store_2d(&maps.du, x, rc, &sh.rawU[s][0][0]);
+    tma_store_2d(&maps.dd, x, rc, &sh.rawD[s][0][0]);
+    if (has_z) tma_store_2d(&maps.dz, x, rc, &sh.rawZ[s][0][0]);
+    bulk_commit();
+  };
+  if (use_tma && tid == 0) {
     mbar_init(&sh.bar[0], 1);
     mbar_init(&sh.bar[1], 1);
     mbar_init(&sh.barP, 1);
     fence_mbar_init();
     if (k_last >= k_begin) {
       issue(0);
-      if (has_z) issue_pre(0);
+      if (kWarps == 1 && has_z) issue_pre(0);
     }
     if (k_last >= k_begin + 1) issue(1);
   }
-  __syncwarp();
+  if constexpr (kWarps > 1) {
+    __syncthreads();
+  } else {
+    __syncwarp();
+  }
 
   // Adjoint carries: g of the step after the current one and its a.
   float gn[kS], an[kS];
@@ -315,6 +348,7 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
     T* bU = &sh.rawU[s][0][0];
     T* bY = &sh.rawY[s][0][0];
     T* bZ = &sh.rawZ[s][0][0];
+    T* bP = &sh.rawP[kWarps > 1 ? s : 0][0][0];
     const float* bB = &sh.rawB[s][0][0];
     const float* bC = &sh.rawC[s][0][0];
     // fp32 work rows: delta_eff and dy
@@ -363,30 +397,41 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
 
     if (use_tma) {
       bool ok = mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1, p.wait_polls);
-      if (has_z) ok = ok && mbar_wait_bounded(&sh.barP, i & 1, p.wait_polls);
-      if (__any_sync(0xffffffffu, !ok)) {
-        if (lane == 0) {
+      if (kWarps == 1 && has_z) ok = ok && mbar_wait_bounded(&sh.barP, i & 1, p.wait_polls);
+      bool give_up;
+      if constexpr (kWarps > 1) {
+        give_up = __syncthreads_or(!ok) != 0;
+      } else {
+        give_up = __any_sync(0xffffffffu, !ok);
+      }
+      if (give_up) {
+        if (tid == 0) {
           atomicOr(&g_bwd_device_error, kErrTmaTimeout);
           // let the copies in flight land before the CTA exits
           mbar_wait_bounded(&sh.bar[s], (i >> 1) & 1);
-          if (has_z) mbar_wait_bounded(&sh.barP, i & 1);
+          if (kWarps == 1 && has_z) mbar_wait_bounded(&sh.barP, i & 1);
           if (i == 0 && k > k_begin) mbar_wait_bounded(&sh.bar[1], 0);
           bulk_wait_all();
         }
         return;
       }
     } else {
-      stage_tile_plain(bD, static_cast<const T*>(p.delta), row0, n_ch, kCh, L, t0, lane);
-      stage_tile_plain(bU, static_cast<const T*>(p.u), row0, n_ch, kCh, L, t0, lane);
-      stage_tile_plain(bY, static_cast<const T*>(p.dout), row0, n_ch, kCh, L, t0, lane);
+      // each warp stages its own channel rows, warp 0 the B and C rows
+      const size_t wrow = row0 + wc0;
+      const int wo = wc0 * kBT;
+      stage_tile_plain(bD + wo, static_cast<const T*>(p.delta), wrow, n_wch, kCPW, L, t0, lane);
+      stage_tile_plain(bU + wo, static_cast<const T*>(p.u), wrow, n_wch, kCPW, L, t0, lane);
+      stage_tile_plain(bY + wo, static_cast<const T*>(p.dout), wrow, n_wch, kCPW, L, t0, lane);
       if (has_z) {
-        stage_tile_plain(bZ, static_cast<const T*>(p.z), row0, n_ch, kCh, L, t0, lane);
-        stage_tile_plain(&sh.rawP[0][0], static_cast<const T*>(p.out_pre), row0, n_ch, kCh, L,
-                         t0, lane);
+        stage_tile_plain(bZ + wo, static_cast<const T*>(p.z), wrow, n_wch, kCPW, L, t0, lane);
+        stage_tile_plain(bP + wo, static_cast<const T*>(p.out_pre), wrow, n_wch, kCPW, L, t0,
+                         lane);
       }
-      const size_t brow = static_cast<size_t>(b) * NS;
-      stage_tile_plain(&sh.rawB[s][0][0], p.B32, brow, NS, NS, L, t0, lane);
-      stage_tile_plain(&sh.rawC[s][0][0], p.C32, brow, NS, NS, L, t0, lane);
+      if (warp == 0) {
+        const size_t brow = static_cast<size_t>(b) * NS;
+        stage_tile_plain(&sh.rawB[s][0][0], p.B32, brow, NS, NS, L, t0, lane);
+        stage_tile_plain(&sh.rawC[s][0][0], p.C32, brow, NS, NS, L, t0, lane);
+      }
       __syncwarp();
     }
 
@@ -402,7 +447,7 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
         float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f), p4 = z4;
         if (has_z) {
           z4 = ld4s(bZ, c, tt);
-          p4 = ld4s(&sh.rawP[0][0], c, tt);
+          p4 = ld4s(bP, c, tt);
         }
         const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
         const float us[4] = {u4.x, u4.y, u4.z, u4.w};
@@ -431,16 +476,31 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
         if (has_z) st4s(bZ, c, tt, make_float4(dz[0], dz[1], dz[2], dz[3]));
       }
     }
-    __syncwarp();
-
-    if (use_tma && lane == 0 && k > k_begin) {
-      fence_proxy_async_smem();  // the warp's reads of rawP are done
-      if (has_z) issue_pre(i + 1);
-      // the other buffer held the previous position's du/ddelta/dz for its
-      // bulk stores; once they have read it, refill it with position i + 1
-      if (i >= 1) {
-        bulk_wait_read_all();
-        issue(i + 1);
+    if constexpr (kWarps > 1) {
+      // the CTA's barrier of the tile: past it every warp is done with
+      // position i - 1 (and, staged by plain loads, warp 0's B and C rows of
+      // this position are visible); its du / ddelta / dz rows, written by
+      // all threads (generic proxy), leave by TMA stores (async proxy)
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (use_tma && tid == 0) {
+        if (i >= 1 && tma_store) store_pos(i - 1);
+        if (k > k_begin && i >= 1) {
+          bulk_wait_read_all();  // the stores have read buffer s ^ 1
+          issue(i + 1);
+        }
+      }
+    } else {
+      __syncwarp();
+      if (use_tma && lane == 0 && k > k_begin) {
+        fence_proxy_async_smem();  // the warp's reads of rawP are done
+        if (has_z) issue_pre(i + 1);
+        // the other buffer held the previous position's du/ddelta/dz for its
+        // bulk stores; once they have read it, refill it with position i + 1
+        if (i >= 1) {
+          bulk_wait_read_all();
+          issue(i + 1);
+        }
       }
     }
 
@@ -650,24 +710,37 @@ __global__ void __launch_bounds__(32, kLPT ? 16 : 0)
       }
     }
 
-    // ---- 4. the tile's du, ddelta, dz
+    // ---- 4. the tile's du, ddelta, dz (multi-warp CTAs with TMA stores:
+    // thread 0 stores them past the next tile's barrier, or below)
     if (tma_store) {
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_2d(&maps.du, t0, rc, bU);
-        tma_store_2d(&maps.dd, t0, rc, bD);
-        if (has_z) tma_store_2d(&maps.dz, t0, rc, bZ);
-        bulk_commit();
+      if constexpr (kWarps == 1) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&maps.du, t0, rc, bU);
+          tma_store_2d(&maps.dd, t0, rc, bD);
+          if (has_z) tma_store_2d(&maps.dz, t0, rc, bZ);
+          bulk_commit();
+        }
       }
     } else {
-      unstage_tile_plain(static_cast<T*>(p.du), bU, row0, n_ch, L, t0, lane);
-      unstage_tile_plain(static_cast<T*>(p.ddelta), bD, row0, n_ch, L, t0, lane);
-      if (has_z) unstage_tile_plain(static_cast<T*>(p.dz), bZ, row0, n_ch, L, t0, lane);
+      const size_t wrow = row0 + wc0;
+      const int wo = wc0 * kBT;
+      unstage_tile_plain(static_cast<T*>(p.du), bU + wo, wrow, n_wch, L, t0, lane);
+      unstage_tile_plain(static_cast<T*>(p.ddelta), bD + wo, wrow, n_wch, L, t0, lane);
+      if (has_z) unstage_tile_plain(static_cast<T*>(p.dz), bZ + wo, wrow, n_wch, L, t0, lane);
       __syncwarp();
     }
   }
-  if (use_tma && lane == 0) bulk_wait_all();
+  if constexpr (kWarps > 1) {
+    // the last position's rows
+    if (tma_store && k_last >= k_begin) {
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) store_pos(k_last - k_begin);
+    }
+  }
+  if (use_tma && tid == 0) bulk_wait_all();
 
   // ---- per-row results
 #pragma unroll
@@ -957,23 +1030,38 @@ static cudaError_t launch_bwd_finish(const BwdParams& p, int dstate, int io_dtyp
                                      void* dB_out, void* dC_out, float* dA, float* dD,
                                      float* ddelta_bias, cudaStream_t stream);
 
-template <int NS, typename T, bool kZOH>
-static cudaError_t launch_bwd_tile_t(const BwdParams& p, const TileMaps& maps,
-                                     cudaStream_t stream) {
+// The scan kernel of kWarps-warp CTAs (plain, longest-first or segmented).
+template <int NS, typename T, bool kZOH, int kWarps>
+static cudaError_t launch_bwd_main(const BwdParams& p, const TileMaps& maps,
+                                   cudaStream_t stream) {
   // the bytes in use: sizeof() would round up to the 1024-byte alignment
-  using Sh = TileShared<NS, T>;
+  using Sh = TileShared<NS, T, kWarps>;
   const size_t smem = offsetof(Sh, barP) + sizeof(uint64_t);
-  auto kern = ss_bwd_tile_kernel<NS, T, kZOH, false>;
+  auto kern = ss_bwd_tile_kernel<NS, T, kZOH, false, false, kWarps>;
   if constexpr (NS == 16 && !kZOH) {
     if (p.seq_lens != nullptr && p.n_seg == 1 && p.batch <= kLongestFirstMax)
-      kern = ss_bwd_tile_kernel<NS, T, kZOH, false, true>;
+      kern = ss_bwd_tile_kernel<NS, T, kZOH, false, true, kWarps>;
   }
+  if (p.n_seg > 1) kern = ss_bwd_tile_kernel<NS, T, kZOH, true, false, kWarps>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const unsigned gx = (p.dim + TileCfg<NS>::kCh - 1) / TileCfg<NS>::kCh;
+  const unsigned gx = (p.dim + Sh::kCh - 1) / Sh::kCh;
+  kern<<<dim3(gx, p.batch, p.n_seg), 32 * kWarps, smem, stream>>>(p, maps);
+  return cudaPeekAtLastError();
+}
+
+// maps: boxes of one warp's channels (the adjoint pass); maps_w: of a
+// kWarps-warp CTA's (the scan kernel; the same as maps for one warp).
+template <int NS, typename T, bool kZOH>
+static cudaError_t launch_bwd_tile_t(const BwdParams& p, const TileMaps& maps,
+                                     const TileMaps& maps_w, int warps, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
   if (p.n_seg > 1) {
     // the segments' seeds: adjoint pass (segments 1 ..), then the combine
+    using Sh = TileShared<NS, T>;
+    const size_t smem = offsetof(Sh, barP) + sizeof(uint64_t);
+    const unsigned gx = (p.dim + TileCfg<NS>::kCh - 1) / TileCfg<NS>::kCh;
     auto kern_adj = ss_bwd_segadj_kernel<NS, T>;
     e = cudaFuncSetAttribute(kern_adj, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
@@ -983,27 +1071,22 @@ static cudaError_t launch_bwd_tile_t(const BwdParams& p, const TileMaps& maps,
     seg_combine_bwd_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
         p.A, p.dlast, p.seg_G, p.seg_dsum, p.seg_carry, p.batch, p.dim, NS, p.n_seg);
   }
-  if (p.n_seg > 1) {
-    auto kern_seg = ss_bwd_tile_kernel<NS, T, kZOH, true>;
-    e = cudaFuncSetAttribute(kern_seg, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    kern_seg<<<dim3(gx, p.batch, p.n_seg), 32, smem, stream>>>(p, maps);
-  } else {
-    kern<<<dim3(gx, p.batch, 1), 32, smem, stream>>>(p, maps);
+  if constexpr (NS == 16) {
+    if (warps == 2) return launch_bwd_main<NS, T, kZOH, 2>(p, maps_w, stream);
   }
-  return cudaPeekAtLastError();
+  return launch_bwd_main<NS, T, kZOH, 1>(p, maps, stream);
 }
 
 template <typename T, bool kZOH>
-static cudaError_t launch_bwd_tile_n(const BwdParams& p, const TileMaps& maps, int dstate,
+static cudaError_t launch_bwd_tile_n(const BwdParams& p, const TileMaps& maps,
+                                     const TileMaps& maps_w, int warps, int dstate,
                                      cudaStream_t stream) {
   switch (dstate) {
-    case 1: return launch_bwd_tile_t<1, T, kZOH>(p, maps, stream);
-    case 2: return launch_bwd_tile_t<2, T, kZOH>(p, maps, stream);
-    case 4: return launch_bwd_tile_t<4, T, kZOH>(p, maps, stream);
-    case 8: return launch_bwd_tile_t<8, T, kZOH>(p, maps, stream);
-    case 16: return launch_bwd_tile_t<16, T, kZOH>(p, maps, stream);
+    case 1: return launch_bwd_tile_t<1, T, kZOH>(p, maps, maps_w, warps, stream);
+    case 2: return launch_bwd_tile_t<2, T, kZOH>(p, maps, maps_w, warps, stream);
+    case 4: return launch_bwd_tile_t<4, T, kZOH>(p, maps, maps_w, warps, stream);
+    case 8: return launch_bwd_tile_t<8, T, kZOH>(p, maps, maps_w, warps, stream);
+    case 16: return launch_bwd_tile_t<16, T, kZOH>(p, maps, maps_w, warps, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1038,11 +1121,39 @@ static bool encode_tile(CUtensorMap* m, const void* base, int io_dtype, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Warps per CTA of the N = 16 scan kernel. Two-warp CTAs share the B and C
+// staging, so that with bf16 I/O 16 warps per SM fit in shared memory (one-
+// warp CTAs: 14); measured, they pay for their barrier per tile only there:
+// configs[2] backward 3.63 -> 3.59 ms, while fp32 (configs[1]: 0.503 ->
+// 0.523 ms) and time-segmented bf16 (configs[4]: 18.0 -> 18.3 ms) lose.
+// MAMBA_SS_BWD_WARPS=1 or 2 forces either (tests).
+static int bwd_warps(int dstate, int io_dtype, int n_seg) {
+  if (dstate != 16) return 1;
+  int w = io_dtype == MSS_BF16 && n_seg == 1 ? 2 : 1;
+  if (const char* env = getenv("MAMBA_SS_BWD_WARPS")) w = atoi(env) == 1 ? 1 : 2;
+  return w;
+}
+
+static bool encode_channel_maps(TileMaps* m, const BwdParams& p, int io_dtype, uint32_t ch) {
+  const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
+  const uint64_t L = p.seqlen;
+  return encode_tile(&m->u, p.u, io_dtype, rows, L, ch) &&
+         encode_tile(&m->d, p.delta, io_dtype, rows, L, ch) &&
+         encode_tile(&m->y, p.dout, io_dtype, rows, L, ch) &&
+         encode_tile(&m->du, p.du, io_dtype, rows, L, ch) &&
+         encode_tile(&m->dd, p.ddelta, io_dtype, rows, L, ch) &&
+         (!p.z || (encode_tile(&m->z, p.z, io_dtype, rows, L, ch) &&
+                   encode_tile(&m->p, p.out_pre, io_dtype, rows, L, ch) &&
+                   encode_tile(&m->dz, p.dz, io_dtype, rows, L, ch)));
+}
+
 static cudaError_t launch_bwd_tile(const BwdParams& p, int dstate, int io_dtype, int zoh,
                                    cudaStream_t stream) {
   BwdParams pk = p;
-  TileMaps maps;
+  TileMaps maps, maps_w;
   memset(&maps, 0, sizeof(maps));
+  memset(&maps_w, 0, sizeof(maps_w));
+  const int warps = bwd_warps(dstate, io_dtype, p.n_seg);
   const size_t esize = io_dtype == MSS_BF16 ? 2 : 4;
   const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   pk.tma_ok = (p.seqlen * esize) % 16 == 0 && al16(p.B32) && al16(p.C32) && al16(p.u) &&
@@ -1050,26 +1161,23 @@ static cudaError_t launch_bwd_tile(const BwdParams& p, int dstate, int io_dtype,
               (!p.z || (al16(p.z) && al16(p.dz) && al16(p.out_pre)));
   if (pk.tma_ok) {
     const uint64_t brows = static_cast<uint64_t>(p.batch) * dstate;
-    const uint64_t rows = static_cast<uint64_t>(p.batch) * p.dim;
     const uint64_t L = p.seqlen;
     const uint32_t ch = static_cast<uint32_t>(tile_channels(dstate));
     const uint32_t ns = static_cast<uint32_t>(dstate);
     pk.tma_ok = encode_tile(&maps.b, p.B32, MSS_F32, brows, L, ns) &&
                 encode_tile(&maps.c, p.C32, MSS_F32, brows, L, ns) &&
-                encode_tile(&maps.u, p.u, io_dtype, rows, L, ch) &&
-                encode_tile(&maps.d, p.delta, io_dtype, rows, L, ch) &&
-                encode_tile(&maps.y, p.dout, io_dtype, rows, L, ch) &&
-                encode_tile(&maps.du, p.du, io_dtype, rows, L, ch) &&
-                encode_tile(&maps.dd, p.ddelta, io_dtype, rows, L, ch) &&
-                (!p.z || (encode_tile(&maps.z, p.z, io_dtype, rows, L, ch) &&
-                          encode_tile(&maps.p, p.out_pre, io_dtype, rows, L, ch) &&
-                          encode_tile(&maps.dz, p.dz, io_dtype, rows, L, ch)));
+                encode_channel_maps(&maps, p, io_dtype, ch);
+    if (pk.tma_ok) {
+      maps_w = maps;
+      if (warps > 1)
+        pk.tma_ok = encode_channel_maps(&maps_w, p, io_dtype, ch * static_cast<uint32_t>(warps));
+    }
   }
   if (io_dtype == MSS_BF16)
-    return zoh ? launch_bwd_tile_n<__nv_bfloat16, true>(pk, maps, dstate, stream)
-               : launch_bwd_tile_n<__nv_bfloat16, false>(pk, maps, dstate, stream);
-  return zoh ? launch_bwd_tile_n<float, true>(pk, maps, dstate, stream)
-             : launch_bwd_tile_n<float, false>(pk, maps, dstate, stream);
+    return zoh ? launch_bwd_tile_n<__nv_bfloat16, true>(pk, maps, maps_w, warps, dstate, stream)
+               : launch_bwd_tile_n<__nv_bfloat16, false>(pk, maps, maps_w, warps, dstate, stream);
+  return zoh ? launch_bwd_tile_n<float, true>(pk, maps, maps_w, warps, dstate, stream)
+             : launch_bwd_tile_n<float, false>(pk, maps, maps_w, warps, dstate, stream);
 }
 
 cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
