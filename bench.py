@@ -315,10 +315,10 @@ class ScanCase:
 
     def launches_per_step(self):
         """Kernels of this library per step: forward 1, backward 2 (tile +
-        parameter reduction), + 2 bf16 narrowings of dB/dC; time segments add
-        the end-state pass and its combine (forward) and the adjoint pass and
-        its combine (backward)."""
-        k = 3 + (2 if self.io.is_floating_point and self.esize == 2 else 0)
+        parameter reduction); bf16 I/O adds the widening of B and C and the
+        two narrowings of dB/dC; time segments add the end-state pass and its
+        combine (forward) and the adjoint pass and its combine (backward)."""
+        k = 3 + (3 if self.esize == 2 else 0)
         if self.ssc._lib().mamba_ss_segments(self.b, self.L, self.d, self.n) > 1:
             k += 4
         return k
