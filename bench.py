@@ -256,6 +256,12 @@ class ScanCase:
     def exchange(self):
         from mamba.distributed import allreduce_bc_grads, allreduce_param_grads
 
+        if os.environ.get("MSS_BENCH_EXCHANGE") == "sync":  # diagnostics: blocking exchange
+            if self.chan:
+                allreduce_bc_grads(self.dB, self.dC)
+            else:
+                allreduce_param_grads(self.params)
+            return
         if self.chan:
             self.work = allreduce_bc_grads(self.dB, self.dC, async_op=True)
         else:
@@ -307,7 +313,15 @@ class ScanCase:
         total = t0.elapsed_time(t1)
         fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
         bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+        self.per_rank = None
         if self.world > 1:
+            # every rank's own figures (its backward includes waiting for the
+            # previous step's exchange, i.e. for the slowest rank)
+            mine = torch.tensor([total, fwd_ms, bwd_ms, float(self.valid_steps)],
+                                device=self.dev)
+            allr = [torch.empty_like(mine) for _ in range(self.world)]
+            dist.all_gather(allr, mine)
+            self.per_rank = [[round(float(v), 4) for v in r.tolist()] for r in allr]
             t = torch.tensor([total], device=self.dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             total = float(t.item())
@@ -374,6 +388,12 @@ def run_gpu(args, cfg):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        # The exchanges are small (110 KB of parameter gradients; 8 MB of
+        # dB/dC for configs[4]). NCCL's NVLink SHARP (NVLS) all-reduce took
+        # about 2.5 ms per call on 8 B200s here (a configs[2] step 4.5 ->
+        # 7.1 ms), its ring/tree algorithms a few tens of microseconds, so
+        # NVLS is off unless the caller's environment says otherwise.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         # NCCL prints its version banner on stdout when the communicator is
         # created; keep stdout for the one JSON line
         with _stdout_to_stderr():
@@ -383,7 +403,12 @@ def run_gpu(args, cfg):
     case = ScanCase(cfg, rank, world, dev)
     sampler = ClockSampler(local)
     total_ms, fwd_ms, bwd_ms = case.time(args.steps, args.warmup, sampler)
+    per_rank = case.per_rank
     clocks = sampler.summary()
+    clocks_per_rank = None
+    if world > 1:
+        clocks_per_rank = [None] * world
+        dist.all_gather_object(clocks_per_rank, {k: clocks.get(k) for k in ("sm_mhz", "reasons")})
     b, d, L, n, esize = case.b, case.d, case.L, case.n, case.esize
     launches = case.launches_per_step() * args.steps
     valid = case.valid_steps / (b * L)
@@ -483,8 +508,13 @@ def run_gpu(args, cfg):
         "roofline_issue": issue,
         "binding": binding,
         "clocks": clocks,
+        "clocks_per_rank": clocks_per_rank,
         "gpu_launches": launches,
     }
+    if per_rank is not None:
+        res["per_rank_ms"] = {"columns": ["total", "fwd", "bwd (incl. the wait for the "
+                                          "previous exchange)", "valid_steps"],
+                              "ranks": per_rank}
     if strong is not None:
         res["channel_sharded"] = strong
     if e2e is not None:
