@@ -155,12 +155,30 @@ struct CplxShared {
   float2 Ct[16][kCT];
 };
 
+// The forward's staging: tiles of kFT steps; delta, u, z and B, C of the next
+// tile are copied in by cp.async (zero-filled past the valid length) while
+// the current tile is scanned.
+constexpr int kFT = 16;
+constexpr int kFRow = kFT + 4;
+template <int kCh>
+struct CplxFwdShared {
+  float dlt[kCh][kFRow];  // delta_eff
+  float uu[kCh][kFRow];   // u (masked)
+  float yy[kCh][kFRow];   // D u, then + y
+  float rD[2][kCh][kFT];  // raw delta, u, z (two buffers)
+  float rU[2][kCh][kFT];
+  float rZ[2][kCh][kFT];
+  float2 Bt[2][16][kFT];
+  float2 Ct[2][16][kFT];
+};
+
 template <int NS, bool kZOH>
 __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
     ss_cfwd_kernel(const CplxParams p) {
   using Cfg = CplxCfg<NS>;
   constexpr int kS = Cfg::kS, kLPC = Cfg::kLPC, kCh = Cfg::kCh, kThreads = Cfg::kThreads;
-  __shared__ CplxShared<kCh> sh;
+  constexpr int kCT = kFT;
+  __shared__ CplxFwdShared<kCh> sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y, d0 = blockIdx.x * kCh;
   const int L = p.seqlen;
@@ -184,27 +202,51 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
     if (act && p.h0) h[j] = cld(static_cast<const float2*>(p.h0) + row * NS + n);
   }
   const size_t bdl = static_cast<size_t>(b) * p.dim * L;
+  const float* zb = p.z ? p.z : p.u;  // a valid address when z is absent
+  // ---- staging of tile t0s into buffer sb (asynchronous, one commit group)
+  auto stage = [&](int t0s, int sb) {
+    for (int i = tid; i < kCh * kCT; i += kThreads) {
+      const int c = i / kCT, tt = i % kCT, t = t0s + tt;
+      const bool v = c < n_ch && t < len;
+      const size_t off = v ? bdl + static_cast<size_t>(d0 + c) * L + t : 0;
+      cp_async4(&sh.rD[sb][c][tt], p.delta + off, v);
+      cp_async4(&sh.rU[sb][c][tt], p.u + off, v);
+      cp_async4(&sh.rZ[sb][c][tt], zb + off, v && p.z != nullptr);
+    }
+    for (int i = tid; i < NS * kCT; i += kThreads) {
+      const int n = i / kCT, tt = i % kCT, t = t0s + tt;
+      const bool v = t < len;
+      const size_t off = v ? static_cast<size_t>(n) * L + t : 0;
+      cp_async8(&sh.Bt[sb][n][tt], B2 + off, v);
+      cp_async8(&sh.Ct[sb][n][tt], C2 + off, v);
+    }
+    cp_async_commit();
+  };
+  stage(0, 0);
   for (int t0 = 0; t0 < L; t0 += kCT) {
-    // ---- stage: delta_eff, u, D u (rows), B and C (states)
+    const int sb = (t0 / kCT) & 1;
+    // the next tile's copies fly while this one is scanned (an empty group
+    // past the end keeps the wait below uniform)
+    if (t0 + kCT < L) {
+      stage(t0 + kCT, sb ^ 1);
+    } else {
+      cp_async_commit();
+    }
+    cp_async_wait<1>();
+    __syncthreads();
+    // ---- transform: delta_eff, u, D u (rows)
     for (int i = tid; i < kCh * kCT; i += kThreads) {
       const int c = i / kCT, tt = i % kCT, t = t0 + tt;
       float dv = 0.f, uv = 0.f, yd = 0.f;
       if (c < n_ch && t < len) {
-        const size_t off = bdl + static_cast<size_t>(d0 + c) * L + t;
-        float x = p.delta[off] + (p.delta_bias ? p.delta_bias[d0 + c] : 0.f);
+        const float x = sh.rD[sb][c][tt] + (p.delta_bias ? p.delta_bias[d0 + c] : 0.f);
         dv = p.delta_softplus ? softplus_f(x) : x;
-        uv = p.u[off];
+        uv = sh.rU[sb][c][tt];
         yd = p.D ? p.D[d0 + c] * uv : 0.f;
       }
       sh.dlt[c][tt] = dv;
       sh.uu[c][tt] = uv;
       sh.yy[c][tt] = yd;
-    }
-    for (int i = tid; i < NS * kCT; i += kThreads) {
-      const int n = i / kCT, tt = i % kCT, t = t0 + tt;
-      const bool v = t < len;
-      sh.Bt[n][tt] = v ? B2[static_cast<size_t>(n) * L + t] : make_float2(0.f, 0.f);
-      sh.Ct[n][tt] = v ? C2[static_cast<size_t>(n) * L + t] : make_float2(0.f, 0.f);
     }
     __syncthreads();
     // ---- scan, one step per iteration (rolled: the per-step body is long);
@@ -230,12 +272,12 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
       for (int j = 0; j < kS; ++j) {
         const int n = q + kLPC * j;
         const Cx a = av[j], bb = bbs[j];
-        const Cx Bn = cld(&sh.Bt[n][tt]);
+        const Cx Bn = cld(&sh.Bt[sb][n][tt]);
         // Euler: b_bar u = delta u B (real times complex)
         const Cx bu = kZOH ? cmul(bb, {Bn.r * uv, Bn.i * uv}) : Cx{dlu * Bn.r, dlu * Bn.i};
         h[j] = {fmaf(a.r, h[j].r, fmaf(-a.i, h[j].i, bu.r)),
                 fmaf(a.r, h[j].i, fmaf(a.i, h[j].r, bu.i))};
-        const Cx Cn = cld(&sh.Ct[n][tt]);
+        const Cx Cn = cld(&sh.Ct[sb][n][tt]);
         yp = fmaf(Cn.r, h[j].r, fmaf(-Cn.i, h[j].i, yp));
       }
 #pragma unroll
@@ -257,7 +299,7 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
       float pre = 0.f, o = 0.f;
       if (t < len) {
         pre = sh.yy[c][tt];
-        o = p.z ? pre * silu_f(p.z[off]) : pre;
+        o = p.z ? pre * silu_f(sh.rZ[sb][c][tt]) : pre;
       }
       p.out[off] = o;
       if (p.out_pre) p.out_pre[off] = pre;
