@@ -23,8 +23,6 @@ namespace mss {
 
 __device__ unsigned int g_cplx_device_error = 0;
 
-constexpr int kCT = 32;    // steps per tile
-constexpr int kCRow = kCT + 4;
 
 template <int NS>
 struct CplxCfg {
@@ -146,14 +144,6 @@ __device__ __forceinline__ void cdisc(float dl, Cx A, Cx& a, Cx& bb) {
   }
 }
 
-template <int kCh>
-struct CplxShared {
-  float dlt[kCh][kCRow];  // delta_eff (rows = channels of the CTA)
-  float uu[kCh][kCRow];   // u (masked)
-  float yy[kCh][kCRow];   // forward: D u, then + y; backward: dy
-  float2 Bt[16][kCT];
-  float2 Ct[16][kCT];
-};
 
 // The forward's staging: tiles of kFT steps; delta, u, z and B, C of the next
 // tile are copied in by cp.async (zero-filled past the valid length) while
@@ -313,13 +303,35 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads)
   }
 }
 
+// The backward's staging: tiles of kGT steps (two groups); delta, u, dout,
+// z, the pre-gate output and B, C of the next tile (to the left) are copied
+// in by cp.async while the current one is processed. Short tiles keep the
+// double buffers within the shared memory that lets 11 one-warp CTAs reside
+// per SM (a configs[1] layer's whole grid in one wave).
+constexpr int kGT = 8;
+constexpr int kGRow = kGT + 4;
+template <int kCh>
+struct CplxBwdShared {
+  float dlt[kCh][kGRow];  // delta_eff
+  float uu[kCh][kGRow];   // u (masked)
+  float yy[kCh][kGRow];   // dy
+  float rD[2][kCh][kGT];  // raw delta, u, dout, z, pre-gate (two buffers)
+  float rU[2][kCh][kGT];
+  float rY[2][kCh][kGT];
+  float rZ[2][kCh][kGT];
+  float rP[2][kCh][kGT];
+  float2 Bt[2][16][kGT];
+  float2 Ct[2][16][kGT];
+};
+
 template <int NS, bool kZOH>
 __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads == 32 ? 11 : 1)
     ss_cbwd_kernel(const CplxParams p) {
   using Cfg = CplxCfg<NS>;
   constexpr int kS = Cfg::kS, kLPC = Cfg::kLPC, kCh = Cfg::kCh, kThreads = Cfg::kThreads;
+  constexpr int kCT = kGT;
   static_assert(Cfg::kWarps == 1, "the channel sums of dB / dC are per warp");
-  __shared__ CplxShared<kCh> sh;
+  __shared__ CplxBwdShared<kCh> sh;
   // one group's dB (re, im) and dC (re, im) per (channel, swizzled state),
   // summed over the warp's channels by flush_part
   __shared__ float4 part[4][kCh][NS];
@@ -363,10 +375,61 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads =
       if (p.dz) p.dz[off] = 0.f;
     }
   }
+  const float* zb = p.z ? p.z : p.u;  // valid addresses when z is absent
+  const float* pb = p.out_pre ? p.out_pre : p.u;
+  // ---- staging of tile t0s into buffer sb (asynchronous, one commit group)
+  auto stage = [&](int t0s, int sb) {
+    for (int i = tid; i < kCh * kCT; i += kThreads) {
+      const int c = i / kCT, tt = i % kCT, t = t0s + tt;
+      const bool v = c < n_ch && t < len;
+      const size_t off = v ? bdl + static_cast<size_t>(d0 + c) * L + t : 0;
+      cp_async4(&sh.rD[sb][c][tt], p.delta + off, v);
+      cp_async4(&sh.rU[sb][c][tt], p.u + off, v);
+      cp_async4(&sh.rY[sb][c][tt], p.dout + off, v);
+      cp_async4(&sh.rZ[sb][c][tt], zb + off, v && p.z != nullptr);
+      cp_async4(&sh.rP[sb][c][tt], pb + off, v && p.z != nullptr);
+    }
+    for (int i = tid; i < NS * kCT; i += kThreads) {
+      const int n = i / kCT, tt = i % kCT, t = t0s + tt;
+      const bool v = t < len;
+      const size_t off = v ? static_cast<size_t>(n) * L + t : 0;
+      cp_async8(&sh.Bt[sb][n][tt], B2 + off, v);
+      cp_async8(&sh.Ct[sb][n][tt], C2 + off, v);
+    }
+    cp_async_commit();
+  };
+  // the state entering group gi (saved carry, or h0)
+  auto load_hs = [&](int gi, Cx (&hs)[kS]) {
+#pragma unroll
+    for (int j = 0; j < kS; ++j) {
+      const int n = q + kLPC * j;
+      hs[j] = {0.f, 0.f};
+      if (act) {
+        if (gi > 0)
+          hs[j] = cld(static_cast<const float2*>(p.chunk_states) +
+                      carry_offset(b, gi - 1, p.n_chunks, p.dim, d, NS) + n);
+        else if (p.h0)
+          hs[j] = cld(static_cast<const float2*>(p.h0) + row * NS + n);
+      }
+    }
+  };
+  if (n_tiles > 0) stage((n_tiles - 1) * kCT, 0);
   for (int k = n_tiles - 1; k >= 0; --k) {
     const int t0 = k * kCT;
+    const int sb = (n_tiles - 1 - k) & 1;
+    __syncthreads();  // every thread is done with buffer sb ^ 1 (the previous tile's)
+    if (k > 0) {
+      stage(t0 - kCT, sb ^ 1);
+    } else {
+      cp_async_commit();
+    }
+    // the carry entering the tile's last valid group, loaded while the copies land
+    const int g_first = min(kCT / 4 - 1, (len - 1 - t0) / 4);
+    Cx hs_next[kS];
+    load_hs((t0 + g_first * 4) / kCkpt, hs_next);
+    cp_async_wait<1>();
     __syncthreads();
-    // ---- stage: delta_eff, u, dy; dz written directly
+    // ---- transform: delta_eff, u, dy; dz written directly
     for (int i = tid; i < kCh * kCT; i += kThreads) {
       const int c = i / kCT, tt = i % kCT, t = t0 + tt;
       float dv = 0.f, uv = 0.f, dy = 0.f;
@@ -374,13 +437,13 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads =
         const size_t off = bdl + static_cast<size_t>(d0 + c) * L + t;
         float dz = 0.f;
         if (t < len) {
-          float x = p.delta[off] + (p.delta_bias ? p.delta_bias[d0 + c] : 0.f);
+          float x = sh.rD[sb][c][tt] + (p.delta_bias ? p.delta_bias[d0 + c] : 0.f);
           dv = p.delta_softplus ? softplus_f(x) : x;
-          uv = p.u[off];
-          dy = p.dout[off];
+          uv = sh.rU[sb][c][tt];
+          dy = sh.rY[sb][c][tt];
           if (p.z) {
-            const float zv = p.z[off], sz = sigmoid_f(zv);
-            dz = dy * p.out_pre[off] * sz * fmaf(zv, 1.f - sz, 1.f);
+            const float zv = sh.rZ[sb][c][tt], sz = sigmoid_f(zv);
+            dz = dy * sh.rP[sb][c][tt] * sz * fmaf(zv, 1.f - sz, 1.f);
             dy *= zv * sz;
           }
         }
@@ -390,32 +453,14 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads =
       sh.uu[c][tt] = uv;
       sh.yy[c][tt] = dy;
     }
-    for (int i = tid; i < NS * kCT; i += kThreads) {
-      const int n = i / kCT, tt = i % kCT, t = t0 + tt;
-      const bool v = t < len;
-      sh.Bt[n][tt] = v ? B2[static_cast<size_t>(n) * L + t] : make_float2(0.f, 0.f);
-      sh.Ct[n][tt] = v ? C2[static_cast<size_t>(n) * L + t] : make_float2(0.f, 0.f);
-    }
     __syncthreads();
     // ---- groups of 4 steps in reverse
-    for (int g = kCT / 4 - 1; g >= 0; --g) {
+    for (int g = g_first; g >= 0; --g) {
       const int tg = g * 4;
-      if (t0 + tg >= len) continue;  // CTA-uniform
-      // the state entering the group (saved carry, or h0)
       Cx hs[kS];
-      const int gi = (t0 + tg) / kCkpt;
 #pragma unroll
-      for (int j = 0; j < kS; ++j) {
-        const int n = q + kLPC * j;
-        hs[j] = {0.f, 0.f};
-        if (act) {
-          if (gi > 0)
-            hs[j] = cld(static_cast<const float2*>(p.chunk_states) +
-                        carry_offset(b, gi - 1, p.n_chunks, p.dim, d, NS) + n);
-          else if (p.h0)
-            hs[j] = cld(static_cast<const float2*>(p.h0) + row * NS + n);
-        }
-      }
+      for (int j = 0; j < kS; ++j) hs[j] = hs_next[j];
+      if (g > 0) load_hs((t0 + tg - 4) / kCkpt, hs_next);
       // recompute a, bb, h over the group (h[e][j] = state after step e)
       Cx aa[4][kS], bbv[4][kS], hh[5][kS];
 #pragma unroll
@@ -436,7 +481,7 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads =
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
           const int n = q + kLPC * j;
-          const Cx Bn = cld(&sh.Bt[n][tg + e]);
+          const Cx Bn = cld(&sh.Bt[sb][n][tg + e]);
           const Cx bu =
               kZOH ? cmul(bbv[e][j], {Bn.r * uv, Bn.i * uv}) : Cx{dlu * Bn.r, dlu * Bn.i};
           const Cx& a = aa[e][j];
@@ -454,8 +499,8 @@ __global__ void __launch_bounds__(CplxCfg<NS>::kThreads, CplxCfg<NS>::kThreads =
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
           const int n = q + kLPC * j;
-          const Cx Cn = cld(&sh.Ct[n][tg + e]);
-          const Cx Bn = cld(&sh.Bt[n][tg + e]);
+          const Cx Cn = cld(&sh.Ct[sb][n][tg + e]);
+          const Cx Bn = cld(&sh.Bt[sb][n][tg + e]);
           // G_t = dy conj(C_t) + conj(a_{t+1}) G_{t+1}
           const Cx Gt = {fmaf(dy, Cn.r, Gp[j].r), fmaf(-dy, Cn.i, Gp[j].i)};
           const Cx& a = aa[e][j];
