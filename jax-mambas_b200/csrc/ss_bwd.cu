@@ -193,10 +193,13 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, 
 // (batch_of_row); its bound of 16 CTAs per SM keeps the registers at the plain
 // kernel's 128 (the ranking code otherwise lifts them to ~170, which cuts the
 // resident warps per SM from 16 to 12). 0 leaves the bound to the compiler.
+// Two-warp CTAs are bounded to 7 per SM: at 8 (128 registers) the compiler
+// spilled 20 bytes and configs[2]'s backward took 3.60 ms, at 7 it does not
+// spill (3.55 ms); the group loop unrolled by 1 or 4 measured 3.59 / 3.96 ms.
 // kWarps: warps per CTA (TileShared); the CTA's kCh channels are kWarps
 // blocks of kCPW, one per warp.
 template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false, int kWarps = 1>
-__global__ void __launch_bounds__(32 * kWarps, kLPT ? 16 / kWarps : 0)
+__global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0)
     ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
   using Cfg = TileCfg<NS>;
   using Sh = TileShared<NS, T, kWarps>;
