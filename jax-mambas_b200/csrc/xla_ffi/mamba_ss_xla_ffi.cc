@@ -36,15 +36,14 @@ ffi::Error ToFfi(mss_status st, const char* where) {
   return ffi::Error(ffi::ErrorCode::kInternal, msg);
 }
 
-ffi::Error CheckResidual(const ffi::AnyBuffer::Dimensions& dims, size_t elems, int32_t batch,
-                         int32_t length, int32_t dim, int32_t dstate) {
+ffi::Error CheckResidual(size_t elems, int32_t batch, int32_t length, int32_t dim,
+                         int32_t dstate) {
   const int64_t need = mamba_ss_chunk_states_elems(batch, length, dim, dstate);
   if (static_cast<int64_t>(elems) < need)
     return ffi::Error(ffi::ErrorCode::kInvalidArgument,
                       "chunk_states must hold mamba_ss_chunk_states_elems() = " +
                           std::to_string(need) + " fp32 elements, got " +
                           std::to_string(elems));
-  (void)dims;
   return ffi::Error::Success();
 }
 
@@ -55,8 +54,7 @@ ffi::Error ForwardImpl(cudaStream_t stream, int32_t discretization, int32_t batc
                        ffi::Buffer<ffi::F32> u, ffi::Buffer<ffi::F32> initial_x,
                        ffi::ResultBuffer<ffi::F32> y, ffi::ResultBuffer<ffi::F32> final_x,
                        ffi::ResultBuffer<ffi::F32> chunk_states) {
-  ffi::Error e = CheckResidual(chunk_states->dimensions(), chunk_states->element_count(),
-                               batch, length, dim, dstate);
+  ffi::Error e = CheckResidual(chunk_states->element_count(), batch, length, dim, dstate);
   if (e.failure()) return e;
   return ToFfi(mamba_ss_fwd(stream, discretization, batch, length, dim, dstate,
                             A.typed_data(), deltas.typed_data(), Bs.typed_data(),
@@ -73,8 +71,7 @@ ffi::Error BenchmarkImpl(cudaStream_t stream, int32_t discretization, int32_t re
                          ffi::Buffer<ffi::F32> u, ffi::Buffer<ffi::F32> initial_x,
                          ffi::ResultBuffer<ffi::F32> y, ffi::ResultBuffer<ffi::F32> final_x,
                          ffi::ResultBuffer<ffi::F32> chunk_states) {
-  ffi::Error e = CheckResidual(chunk_states->dimensions(), chunk_states->element_count(),
-                               batch, length, dim, dstate);
+  ffi::Error e = CheckResidual(chunk_states->element_count(), batch, length, dim, dstate);
   if (e.failure()) return e;
   return ToFfi(mamba_ss_fwd_bench(stream, discretization, repeats, batch, length, dim, dstate,
                                   A.typed_data(), deltas.typed_data(), Bs.typed_data(),
