@@ -400,6 +400,10 @@ def run_gpu(args, cfg):
             dist.init_process_group("nccl", device_id=dev)
             dist.barrier()
 
+    if args.deterministic:
+        from mamba.selective_scan_cuda import set_deterministic
+
+        set_deterministic(True)
     case = ScanCase(cfg, rank, world, dev)
     sampler = ClockSampler(local)
     total_ms, fwd_ms, bwd_ms = case.time(args.steps, args.warmup, sampler)
@@ -489,7 +493,7 @@ def run_gpu(args, cfg):
         "vs_baseline": None, "dtype": cfg["dtype"],
         "data": "synthetic (seeded N(0,1)/U(-4,-2) inputs of the config)",
         "value_all_positions": round(value_all, 3),
-        "config": _config_block(cfg, world),
+        "config": dict(_config_block(cfg, world), deterministic_dBdC=bool(args.deterministic)),
         "kernels_ms": {"fwd": round(fwd_ms, 4), "bwd": round(bwd_ms, 4)},
         "roofline": {"bound": "hbm", "kernel": "ss_bwd_tile_kernel",
                      "achieved": round(bwd_gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -958,6 +962,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-strong", dest="strong", action="store_false",
                     help="skip the channel-sharded configs[4] single-sequence leg")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="bitwise-reproducible dB/dC (partials summed in a fixed order)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU in place of the config's (small profiling cases)")

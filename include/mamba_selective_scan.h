@@ -56,6 +56,22 @@ const char* mamba_ss_version(void);
  * reference, whose kernels have no waits. */
 uint32_t mamba_ss_take_device_error(void);
 
+/* Deterministic dB and dC (process-wide, default off). The backward sums
+ * dB and dC over channels; by default every warp adds its 8-channel sum into
+ * fp32 accumulators with atomics, so the order of the additions, and the last
+ * bits of dB / dC, vary from run to run (as the reference's per-element
+ * atomicAdd, native/upstream_mamba/selective_scan_bwd_kernel.cuh:315-316).
+ * With deterministic mode on, each warp writes its sum to a partial buffer
+ * of the workspace (batch * ceil(dim / channels per warp) * 2 * dstate *
+ * length fp32) and a second kernel adds the partials in a fixed order, so dB
+ * and dC are bitwise reproducible; every other output already is. It costs
+ * that extra traffic (measured: configs[2] backward 3.55 -> 4.32 ms,
+ * configs[1] 0.51 -> 0.60 ms). It changes
+ * mamba_ss_bwd_workspace_bytes: query the size after setting the mode. The
+ * complex scan is not affected. */
+void mamba_ss_set_deterministic(int32_t on);
+int32_t mamba_ss_deterministic(void);
+
 /* Test hook for the bounded waits: sets the number of polls after which
  * the scan kernels launched from now on (any host thread) give up waiting
  * for a tile's TMA staging, report bit 0 through

@@ -340,8 +340,14 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
   float dD_acc = 0.f, dbias_acc = 0.f;
   const bool acc_aligned = (L & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.dB_acc) |
                                               reinterpret_cast<uintptr_t>(p.dC_acc)) & 15) == 0;
-  float* dB_b = p.dB_acc + static_cast<size_t>(b) * NS * L;
-  float* dC_b = p.dC_acc + static_cast<size_t>(b) * NS * L;
+  // deterministic mode: this warp's column of the partial sums instead of
+  // the accumulators, written instead of added
+  const bool det = p.dBC_part != nullptr;
+  const int col = static_cast<int>(blockIdx.x) * kWarps + warp;
+  float* const part_b =
+      det ? p.dBC_part + static_cast<size_t>(b * p.n_cols + col) * 2 * NS * L : nullptr;
+  float* dB_b = det ? part_b : p.dB_acc + static_cast<size_t>(b) * NS * L;
+  float* dC_b = det ? part_b + static_cast<size_t>(NS) * L : p.dC_acc + static_cast<size_t>(b) * NS * L;
 
   for (int k = k_last; k >= k_begin; --k) {
     const int i = k_last - k;
@@ -690,17 +696,28 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
         if (live) {
           float* gp = acc_row + tg;
           if (whole) {
-            atomicAdd(reinterpret_cast<float4*>(gp), keep);
+            if (det) {
+              *reinterpret_cast<float4*>(gp) = keep;
+            } else {
+              atomicAdd(reinterpret_cast<float4*>(gp), keep);
+            }
           } else {
             const float e4[4] = {keep.x, keep.y, keep.z, keep.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (t0 + tg + e < len) atomicAdd(gp + e, e4[e]);
+            for (int e = 0; e < 4; ++e) {
+              if (t0 + tg + e < len) {
+                if (det) {
+                  gp[e] = e4[e];
+                } else {
+                  atomicAdd(gp + e, e4[e]);
+                }
+              }
+            }
           }
         }
       } else {
         __syncwarp();
-        if (live) flush_part<NS>(sh.part, dB_b, L, t0 + tg, len, whole, lane);
+        if (live) flush_part<NS>(sh.part, dB_b, L, t0 + tg, len, whole, lane, det);
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < kS; ++j) {
@@ -708,7 +725,7 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
           sh.part[c][n ^ Cfg::part_swz(c)] = dCq[j];
         }
         __syncwarp();
-        if (live) flush_part<NS>(sh.part, dC_b, L, t0 + tg, len, whole, lane);
+        if (live) flush_part<NS>(sh.part, dC_b, L, t0 + tg, len, whole, lane, det);
         __syncwarp();
       }
     }
@@ -1009,6 +1026,33 @@ cudaError_t launch_param_reduce(const float* dA_part, const float* dD_part,
   return cudaPeekAtLastError();
 }
 
+// Deterministic mode: dB and dC of (batch, dstate, step) as the sum of the
+// warp columns' partials in column order (zero past a sequence's valid
+// length, where no column wrote). One thread per output element; blockIdx.y
+// picks dB (0) or dC (1).
+__global__ void reduce_bc_kernel(const float* __restrict__ part,
+                                 const int32_t* __restrict__ seq_lens, float* __restrict__ dB,
+                                 float* __restrict__ dC, int batch, int dstate, int L,
+                                 int n_cols) {
+  const size_t nl = static_cast<size_t>(dstate) * L;
+  const size_t total = static_cast<size_t>(batch) * nl;
+  const int which = blockIdx.y;
+  float* out = which == 0 ? dB : dC;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / nl);
+    const size_t r = i % nl;  // state * L + t
+    const int t = static_cast<int>(r % L);
+    const int len = seq_lens ? max(0, min(L, seq_lens[b])) : L;
+    float acc = 0.f;
+    if (t < len) {
+      const float* src = part + (static_cast<size_t>(b) * n_cols * 2 + which) * nl + r;
+      for (int c = 0; c < n_cols; ++c) acc += src[static_cast<size_t>(c) * 2 * nl];
+    }
+    out[i] = acc;
+  }
+}
+
 // B and C widened to fp32 for the scan kernels (bf16 I/O): blockIdx.y picks
 // the array; exact (a bf16 is the upper half of an fp32).
 __global__ void bf16_to_f32_pair_kernel(const __nv_bfloat16* __restrict__ B,
@@ -1187,10 +1231,13 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
                        void* dB_out, void* dC_out, float* dA, float* dD,
                        float* ddelta_bias, cudaStream_t stream) {
   const size_t n_bnl = static_cast<size_t>(p.batch) * dstate * p.seqlen;
-  cudaError_t e = cudaMemsetAsync(p.dB_acc, 0, n_bnl * sizeof(float), stream);
-  if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(p.dC_acc, 0, n_bnl * sizeof(float), stream);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
+  if (!p.dBC_part) {  // deterministic mode writes every accumulator element itself
+    e = cudaMemsetAsync(p.dB_acc, 0, n_bnl * sizeof(float), stream);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(p.dC_acc, 0, n_bnl * sizeof(float), stream);
+    if (e != cudaSuccess) return e;
+  }
 
   if (io_dtype == MSS_BF16) {
     const int threads = 256;
@@ -1204,6 +1251,15 @@ cudaError_t launch_bwd(const BwdParams& p, int dstate, int io_dtype, int zoh,
   }
   e = launch_bwd_tile(p, dstate, io_dtype, zoh, stream);
   if (e != cudaSuccess) return e;
+  if (p.dBC_part) {
+    const int threads = 256;
+    const unsigned blocks = static_cast<unsigned>(
+        std::min<size_t>((n_bnl + threads - 1) / threads, 148 * 16));
+    reduce_bc_kernel<<<dim3(blocks, 2), threads, 0, stream>>>(
+        p.dBC_part, p.seq_lens, p.dB_acc, p.dC_acc, p.batch, dstate, p.seqlen, p.n_cols);
+    e = cudaPeekAtLastError();
+    if (e != cudaSuccess) return e;
+  }
   return launch_bwd_finish(p, dstate, io_dtype, dB_out, dC_out, dA, dD, ddelta_bias, stream);
 }
 

@@ -20,6 +20,9 @@ thread_local std::string g_last_error;
 // mamba_ss_debug_set_wait_polls)
 std::atomic<uint32_t> g_wait_polls{mss::kWaitPolls};
 
+// deterministic dB / dC (mamba_ss_set_deterministic)
+std::atomic<int> g_deterministic{0};
+
 mss_status fail(mss_status code, const std::string& msg) {
   g_last_error = msg;
   return code;
@@ -60,7 +63,8 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 struct BwdWorkspace {
   int n_seg, seg_tiles;
   size_t dA_part, dD_part, dbias_part, seg_G, seg_dsum, seg_carry, dB_acc, dC_acc, B32, C32,
-      total;
+      dBC_part, total;
+  int n_cols;
 };
 
 BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
@@ -100,6 +104,13 @@ BwdWorkspace bwd_layout(int batch, int length, int dim, int dstate,
     off += bnl;
     w.C32 = off;
     off += bnl;
+  }
+  // deterministic mode: per warp-column partials of dB and dC
+  w.dBC_part = 0;
+  w.n_cols = (dim + mss::scan_channels_per_cta(dstate) - 1) / mss::scan_channels_per_cta(dstate);
+  if (g_deterministic.load(std::memory_order_relaxed)) {
+    w.dBC_part = off;
+    off += align256(sizeof(float) * static_cast<size_t>(batch) * w.n_cols * 2 * dstate * length);
   }
   w.total = off;
   return w;
@@ -150,6 +161,12 @@ const char* mamba_ss_version(void) { return "mamba-ss-b200 0.1 sm_100a"; }
 uint32_t mamba_ss_take_device_error(void) {
   return mss::take_fwd_device_error() | mss::take_bwd_device_error();
 }
+
+void mamba_ss_set_deterministic(int32_t on) {
+  g_deterministic.store(on ? 1 : 0, std::memory_order_relaxed);
+}
+
+int32_t mamba_ss_deterministic(void) { return g_deterministic.load(std::memory_order_relaxed); }
 
 void mamba_ss_debug_set_wait_polls(int64_t polls) {
   g_wait_polls.store(polls < 0 ? mss::kWaitPolls
@@ -295,6 +312,8 @@ mss_status mamba_ss_fused_bwd(
     p.C32 = static_cast<float*>(const_cast<void*>(C));
   }
   p.dh0 = dinitial_state;
+  p.n_cols = w.n_cols;
+  p.dBC_part = w.dBC_part ? reinterpret_cast<float*>(ws + w.dBC_part) : nullptr;
   cudaError_t e = mss::launch_bwd(p, dstate, io_dtype, discretization, dB, dC,
                                   dA, D ? dD : nullptr,
                                   delta_bias ? ddelta_bias : nullptr,

@@ -121,6 +121,11 @@ struct BwdParams {
   // inputs themselves for fp32 I/O, a copy widened by the launcher for bf16
   float* B32;
   float* C32;
+  // deterministic mode: per warp-column partial sums of dB and dC,
+  // (batch, n_cols, 2, dstate, L) fp32, written (not added) by the scan
+  // kernel and summed in a fixed order by reduce_bc_kernel; null otherwise
+  float* dBC_part;
+  int n_cols;      // warp columns: ceil(dim / channels per warp)
   float* dB_acc;   // fp32 (batch, dstate, L), zeroed before the launch
   float* dC_acc;
   float* dA_part;  // fp32 (n_seg, batch, dim, dstate): per-batch partial sums
@@ -442,7 +447,7 @@ __device__ __forceinline__ int part_swz(int c) {
 // 32/NS lanes of a state combine with xor-shuffles.
 template <int NS>
 __device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_b, int L, int t,
-                                           int len, bool whole, int lane) {
+                                           int len, bool whole, int lane, bool store = false) {
   constexpr int kS = NS < 4 ? NS : 4;  // states per lane
   const int o = lane % NS, h = lane / NS;
   float2 lo = make_float2(0.f, 0.f), hi = lo;
@@ -463,12 +468,24 @@ __device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_
   if (h == 0) {
     float* gp = acc_b + static_cast<size_t>(o) * L + t;
     if (whole) {
-      atomicAdd(reinterpret_cast<float4*>(gp), make_float4(lo.x, lo.y, hi.x, hi.y));
+      const float4 v4 = make_float4(lo.x, lo.y, hi.x, hi.y);
+      if (store) {
+        *reinterpret_cast<float4*>(gp) = v4;
+      } else {
+        atomicAdd(reinterpret_cast<float4*>(gp), v4);
+      }
     } else {
       const float e4[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (t + e < len) atomicAdd(gp + e, e4[e]);
+      for (int e = 0; e < 4; ++e) {
+        if (t + e < len) {
+          if (store) {
+            gp[e] = e4[e];
+          } else {
+            atomicAdd(gp + e, e4[e]);
+          }
+        }
+      }
     }
   }
 }

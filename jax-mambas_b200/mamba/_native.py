@@ -97,6 +97,8 @@ SIGNATURES = {
     ),
     "mamba_ss_segments": (_i32, [_i32, _i32, _i32, _i32]),
     "mamba_ss_debug_set_wait_polls": (None, [ctypes.c_int64]),
+    "mamba_ss_set_deterministic": (None, [_i32]),
+    "mamba_ss_deterministic": (_i32, []),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,

@@ -135,6 +135,19 @@ def _validate_inputs(A, deltas, Bs, Cs, u, initial_x):
 # --------------------------------------------------------------------------
 # Raw launches (device tensors in kernel layout, outputs preallocated)
 # --------------------------------------------------------------------------
+def set_deterministic(on=True):
+    """Make dB and dC of every later backward bitwise reproducible (per-warp
+    partial sums added in a fixed order by a second kernel, instead of fp32
+    atomics in arrival order), or restore the default. Process-wide; costs
+    the partials' extra memory traffic. Workspaces sized before the switch
+    are too small for a deterministic backward."""
+    _lib().mamba_ss_set_deterministic(1 if on else 0)
+
+
+def is_deterministic():
+    return bool(_lib().mamba_ss_deterministic())
+
+
 def chunk_states_elems(batch, length, dim, dstate):
     return int(_lib().mamba_ss_chunk_states_elems(batch, length, dim, dstate))
 
