@@ -480,9 +480,20 @@ def run_gpu(args, cfg):
                  "source": counts.get("source", "profiles/ncu_counts.json")}
     fracs = {"bwd": {"hbm": bwd_gbs / hbm, "sfu": mufu_bwd / mufu_peak},
              "fwd": {"hbm": fwd_gbs / hbm, "sfu": mufu_fwd / mufu_peak}}
+    fp32 = None
     if issue:
         fracs["bwd"]["issue"] = issue["bwd_frac"]
         fracs["fwd"]["issue"] = issue["fwd_frac"]
+        if "fp32_ops_per_valid_elem" in kb:
+            fp32_peak = 148 * 128 * f_mhz * 1e6  # fp32 lanes per SM per clock
+            ob = kb["fp32_ops_per_valid_elem"] * valid_elems / (bwd_ms * 1e-3)
+            of = kf["fp32_ops_per_valid_elem"] * valid_elems / (fwd_ms * 1e-3)
+            fp32 = {"bound": "fp32", "unit": "fp32 op/s", "peak": fp32_peak, "clock_mhz": f_mhz,
+                    "ops_per_elem": {"fwd": kf["fp32_ops_per_valid_elem"],
+                                     "bwd": kb["fp32_ops_per_valid_elem"]},
+                    "bwd_frac": round(ob / fp32_peak, 4), "fwd_frac": round(of / fp32_peak, 4)}
+            fracs["bwd"]["fp32"] = fp32["bwd_frac"]
+            fracs["fwd"]["fp32"] = fp32["fwd_frac"]
     # the binding ceiling of a kernel is the resource it uses the largest share of
     binding = {k: {"resource": max(v, key=v.get), "frac": round(max(v.values()), 4)}
                for k, v in fracs.items()}
@@ -510,6 +521,7 @@ def run_gpu(args, cfg):
                          "fwd_frac": round(mufu_fwd / mufu_peak, 4),
                          "ops_per_elem": {"fwd": mufu_f, "bwd": mufu_b}},
         "roofline_issue": issue,
+        "roofline_fp32": fp32,
         "binding": binding,
         "clocks": clocks,
         "clocks_per_rank": clocks_per_rank,
