@@ -125,16 +125,23 @@ SegPlan seg_plan(int batch, int length, int dim, int dstate) {
   const int n_tiles = (length + kScanTile - 1) / kScanTile;
   const int ch = scan_channels_per_cta(dstate);
   const long long ctas = static_cast<long long>(batch) * ((dim + ch - 1) / ch);
-  // about 11 CTAs per SM are resident; more segments than one wave's worth
-  // still pay (shorter, better balanced work units) until the adjoint and
-  // end-state passes (which re-read most of the inputs) dominate; segments
-  // of at least 8 tiles
-  constexpr long long kTarget = 148 * 18;
+  // Segments only when the grid is short of work: under about 9 one-warp
+  // CTAs per SM (a configs[1] layer, 10.4 per SM, runs faster unsegmented:
+  // the end-state and adjoint passes cost more than the added warps return).
+  // Then many short segments: measured on configs[4]'s single sequence
+  // (640 CTAs), 2 / 3 / 4 / 6 / 12 / 24 segments gave 20.5 / 24.2 / 23.2 /
+  // 26.9 / 27.5 / 27.9 Gelem/s, i.e. finer, better balanced work units keep
+  // paying long after one wave is full, and the extra passes' cost does not
+  // grow with the count. So aim for about 100 CTAs per SM, with segments of
+  // at least 8 tiles.
+  constexpr long long kSegmentBelow = 148 * 9;
+  constexpr long long kTarget = 148 * 100;
   int n = 1;
   if (const char* env = getenv("MAMBA_SS_SEGMENTS")) {
     n = std::max(1, atoi(env));
-  } else if (ctas < kTarget / 2) {
-    n = static_cast<int>(std::min<long long>(kTarget / std::max(1LL, ctas), n_tiles / 8));
+  } else if (ctas < kSegmentBelow) {
+    const long long want = (kTarget + ctas - 1) / std::max(1LL, ctas);
+    n = static_cast<int>(std::min<long long>(want, n_tiles / 8));
   }
   n = std::max(1, std::min(n, n_tiles));
   SegPlan sp;
