@@ -392,8 +392,13 @@ def run_gpu(args, cfg):
         # dB/dC for configs[4]). NCCL's NVLink SHARP (NVLS) all-reduce took
         # about 2.5 ms per call on 8 B200s here (a configs[2] step 4.5 ->
         # 7.1 ms), its ring/tree algorithms a few tens of microseconds, so
-        # NVLS is off unless the caller's environment says otherwise.
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        # NVLS is off (MSS_BENCH_NVLS=1 keeps the environment's setting; a
+        # default from the environment is not trusted: the pool's boxes may
+        # set one).
+        if os.environ.get("MSS_BENCH_NVLS") != "1":
+            os.environ["NCCL_NVLS_ENABLE"] = "0"
+        print(f"rank {rank}: NCCL_NVLS_ENABLE={os.environ.get('NCCL_NVLS_ENABLE')}",
+              file=sys.stderr)
         # NCCL prints its version banner on stdout when the communicator is
         # created; keep stdout for the one JSON line
         with _stdout_to_stderr():
