@@ -56,6 +56,26 @@ const char* mamba_ss_version(void);
  * reference, whose kernels have no waits. */
 uint32_t mamba_ss_take_device_error(void);
 
+/* Debug bounds build (libmamba_ss_b200_bounds.so, compiled with
+ * -DMSS_BOUNDS_CHECK; CMake option MAMBA_SS_DEBUG_BOUNDS). Its forward and
+ * backward scan kernels check every computed global index, and every TMA
+ * store coordinate, against the extent of its array before the access; an
+ * index outside it is counted and the access skipped instead of faulting.
+ * No counterpart in the reference, which has no such build; it stands in
+ * for compute-sanitizer, which is not available on every machine.
+ *   mamba_ss_bounds_checked()  1 in the bounds build, 0 in the normal one.
+ *   mamba_ss_take_bounds_violations(first)  synchronous; returns and clears
+ *     the number of violations since the last call; if first is not NULL it
+ *     receives {site, index, extent} of the first one (site numbers are the
+ *     BoundsSite values of csrc/ss_common.cuh). Always 0 in the normal build.
+ *   mamba_ss_bounds_selftest()  launches one thread that checks an index
+ *     past its extent without any memory access, so that the next
+ *     mamba_ss_take_bounds_violations() returns 1 with site 99 in the bounds
+ *     build (0 in the normal one). */
+int32_t mamba_ss_bounds_checked(void);
+uint64_t mamba_ss_take_bounds_violations(int64_t* first);
+mss_status mamba_ss_bounds_selftest(void);
+
 /* Deterministic dB and dC (process-wide, default off). The backward sums
  * dB and dC over channels; by default every warp adds its 8-channel sum into
  * fp32 accumulators with atomics, so the order of the additions, and the last

@@ -4,6 +4,13 @@ Each ``csrc/*.cu`` file is compiled by nvcc for sm_100a only and linked into
 one shared library next to this file (``lib/``), so the library travels with
 the source tree. Run ``python jax-mambas_b200/build.py`` or call
 ``build_library()``.
+
+``build_library(bounds=True)`` (``build.py --bounds``) builds the debug bounds
+library ``libmamba_ss_b200_bounds.so`` from the same sources with
+``-DMSS_BOUNDS_CHECK``: its scan kernels check every computed global index
+against its array's extent and report violations through
+``mamba_ss_take_bounds_violations()`` instead of faulting. Load it in place of
+the normal library with ``MAMBA_SS_B200_LIB``.
 """
 from __future__ import annotations
 
@@ -18,7 +25,9 @@ PKG_ROOT = Path(__file__).resolve().parent
 CSRC = PKG_ROOT / "csrc"
 LIB_DIR = PKG_ROOT / "lib"
 LIB_NAME = "libmamba_ss_b200.so"
+BOUNDS_LIB_NAME = "libmamba_ss_b200_bounds.so"
 BUILD_DIR = PKG_ROOT / "_build"
+BOUNDS_BUILD_DIR = PKG_ROOT / "_build_bounds"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -50,8 +59,8 @@ def _headers() -> list[Path]:
     )
 
 
-def library_path() -> Path:
-    return LIB_DIR / LIB_NAME
+def library_path(bounds: bool = False) -> Path:
+    return LIB_DIR / (BOUNDS_LIB_NAME if bounds else LIB_NAME)
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:
@@ -61,18 +70,20 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build_library(force: bool = False, verbose: bool = False) -> Path:
+def build_library(force: bool = False, verbose: bool = False, bounds: bool = False) -> Path:
     nvcc = _nvcc()
-    BUILD_DIR.mkdir(exist_ok=True)
+    build_dir = BOUNDS_BUILD_DIR if bounds else BUILD_DIR
+    build_dir.mkdir(exist_ok=True)
     LIB_DIR.mkdir(exist_ok=True)
     headers = _headers()
+    extra = ["-DMSS_BOUNDS_CHECK"] if bounds else []
     objs = []
     jobs = []
     for src in _sources():
-        obj = BUILD_DIR / (src.stem + ".o")
+        obj = build_dir / (src.stem + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + headers):
-            cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+            cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
             jobs.append((src, cmd))
 
     def run(job):
@@ -86,12 +97,12 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
                 raise RuntimeError(
                     f"nvcc failed for {src.name}:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}"
                 )
-            log = BUILD_DIR / (src.stem + ".ptxas.txt")
+            log = build_dir / (src.stem + ".ptxas.txt")
             log.write_text(r.stdout + r.stderr)
             if verbose:
                 sys.stdout.write(r.stderr)
 
-    lib = library_path()
+    lib = library_path(bounds)
     if force or jobs or _stale(lib, objs):
         cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(lib), *map(str, objs), "-lcuda"]
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -101,4 +112,5 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
 
 
 if __name__ == "__main__":
-    print(build_library(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_library(force="--force" in sys.argv, verbose="-v" in sys.argv,
+                        bounds="--bounds" in sys.argv))

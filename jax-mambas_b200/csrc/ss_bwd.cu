@@ -149,11 +149,15 @@ __device__ __forceinline__ void st1s(T* tile, int r, int t, float v) {
 // rows at or past n_valid and steps at or past L read as zero (one warp).
 template <typename T>
 __device__ void stage_tile_plain(T* tile, const T* base, size_t row0, int n_valid, int box_rows,
-                                 int L, int t0, int lane) {
+                                 int L, int t0, int lane, long long extent) {
+  (void)extent;  // element count of base (bounds build)
   for (int i = lane; i < box_rows * kBT; i += 32) {
     const int r = i / kBT, t = i % kBT;
     T v = static_cast<T>(0.f);
-    if (r < n_valid && t0 + t < L) v = base[(row0 + r) * static_cast<size_t>(L) + t0 + t];
+    if (r < n_valid && t0 + t < L
+        MSS_AND(in_bounds(static_cast<long long>((row0 + r) * static_cast<size_t>(L) + t0 + t),
+                          extent, kSiteRowIn)))
+      v = base[(row0 + r) * static_cast<size_t>(L) + t0 + t];
     tile[sw_idx(tile, r, t)] = v;
   }
 }
@@ -161,10 +165,14 @@ __device__ void stage_tile_plain(T* tile, const T* base, size_t row0, int n_vali
 // Plain stores of a staged tile's rows below n_valid, steps below L (one warp).
 template <typename T>
 __device__ void unstage_tile_plain(T* base, const T* tile, size_t row0, int n_valid, int L,
-                                   int t0, int lane) {
+                                   int t0, int lane, long long extent) {
+  (void)extent;  // element count of base (bounds build)
   for (int i = lane; i < n_valid * kBT; i += 32) {
     const int r = i / kBT, t = i % kBT;
-    if (t0 + t < L) base[(row0 + r) * static_cast<size_t>(L) + t0 + t] = tile[sw_idx(tile, r, t)];
+    if (t0 + t < L
+        MSS_AND(in_bounds(static_cast<long long>((row0 + r) * static_cast<size_t>(L) + t0 + t),
+                          extent, kSiteRowOut)))
+      base[(row0 + r) * static_cast<size_t>(L) + t0 + t] = tile[sw_idx(tile, r, t)];
   }
 }
 
@@ -172,16 +180,21 @@ __device__ void unstage_tile_plain(T* base, const T* tile, size_t row0, int n_va
 // when `vec` (from and to multiples of 16 bytes).
 template <typename T>
 __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, bool vec,
-                          int lane) {
+                          int lane, long long extent) {
+  (void)extent;  // element count of base (bounds build)
   if (from >= to) return;
   constexpr int kPer = 16 / sizeof(T);
   for (int r = 0; r < n; ++r) {
     T* rowp = base + (row0 + r) * static_cast<size_t>(L);
     if (vec) {
       for (int t = from + lane * kPer; t < to; t += 32 * kPer)
+        MSS_IF(in_array(rowp + t, base, extent, kSiteRowOut) &&
+               in_array(rowp + t + kPer - 1, base, extent, kSiteRowOut))
         *reinterpret_cast<uint4*>(rowp + t) = make_uint4(0u, 0u, 0u, 0u);
     } else {
-      for (int t = from + lane; t < to; t += 32) rowp[t] = static_cast<T>(0.f);
+      for (int t = from + lane; t < to; t += 32)
+        MSS_IF(in_array(rowp + t, base, extent, kSiteRowOut))
+        rowp[t] = static_cast<T>(0.f);
     }
   }
 }
@@ -237,7 +250,12 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
   auto st_of = [&](int j) { return q + kLPC * (j ^ perm); };
 
   int len = L;
-  if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
+  if (p.seq_lens MSS_AND(in_bounds(b, p.batch, kSiteSeqLens)))
+    len = max(0, min(L, p.seq_lens[b]));
+  // extents of the arrays, in elements (the staging helpers check against
+  // them in the bounds build only)
+  const long long n_bd = static_cast<long long>(p.batch) * p.dim;
+  const long long n_rows = n_bd * L, n_bc = static_cast<long long>(p.batch) * NS * L;
   // this CTA's time segment: tiles [k_begin, k_end); k_last is the last tile
   // of it with valid steps (k_last < k_begin: none)
   const int seg = kSeg ? static_cast<int>(blockIdx.z) : 0;
@@ -253,20 +271,22 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
   float Av[kS], a2[kS];
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
-    Av[j] = __ldg(p.A + d * NS + st_of(j));
+    Av[j] = MSS_SEL(in_bounds(d * NS + st_of(j), static_cast<long long>(p.dim) * NS, kSiteA),
+                    __ldg(p.A + d * NS + st_of(j)), 0.f);
     a2[j] = Av[j] * kLog2e;
   }
-  const float Dv = p.D ? __ldg(p.D + d) : 0.f;
-  const float bias = p.delta_bias ? __ldg(p.delta_bias + d) : 0.f;
+  const float Dv = p.D MSS_AND(in_bounds(d, p.dim, kSiteD)) ? __ldg(p.D + d) : 0.f;
+  const float bias =
+      p.delta_bias MSS_AND(in_bounds(d, p.dim, kSiteBias)) ? __ldg(p.delta_bias + d) : 0.f;
 
   // Steps past the last valid tile are padding: their gradients are zero.
   {
     const int tz = max(k_last + 1, k_begin) * kBT;
     const int te = min(k_end * kBT, L);
     const bool vec = use_tma;  // 16-byte aligned rows (L * esize % 16 == 0)
-    zero_rows(static_cast<T*>(p.du), row0 + wc0, n_wch, L, tz, te, vec, lane);
-    zero_rows(static_cast<T*>(p.ddelta), row0 + wc0, n_wch, L, tz, te, vec, lane);
-    if (has_z) zero_rows(static_cast<T*>(p.dz), row0 + wc0, n_wch, L, tz, te, vec, lane);
+    zero_rows(static_cast<T*>(p.du), row0 + wc0, n_wch, L, tz, te, vec, lane, n_rows);
+    zero_rows(static_cast<T*>(p.ddelta), row0 + wc0, n_wch, L, tz, te, vec, lane, n_rows);
+    if (has_z) zero_rows(static_cast<T*>(p.dz), row0 + wc0, n_wch, L, tz, te, vec, lane, n_rows);
   }
 
   // TMA pipeline: position i of the walk is tile k_last - i; its arrays go
@@ -301,6 +321,8 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
   auto store_pos = [&](int i) {
     const int s = i & 1;
     const int x = (k_last - i) * kBT;
+    MSS_BOUNDS_ONLY(if (!in_bounds(x, L, kSiteTmaStore) ||
+                        !in_bounds(rc + kCh - 1, n_bd, kSiteTmaStore)) return;)
     tma_store_2d(&maps.du, x, rc, &sh.rawU[s][0][0]);
     tma_store_2d(&maps.dd, x, rc, &sh.rawD[s][0][0]);
     if (has_z) tma_store_2d(&maps.dz, x, rc, &sh.rawZ[s][0][0]);
@@ -331,9 +353,11 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
     // the last segment starts from dlast, the others from the carry their
     // right neighbours pass
     if (kSeg && seg < n_seg - 1)
-      gn[j] = act ? p.seg_carry[seg_row * NS + st_of(j)] : 0.f;
+      gn[j] = act MSS_AND(in_bounds(seg_row * NS + st_of(j), n_bd * n_seg * NS, kSiteSegCarry))
+                  ? p.seg_carry[seg_row * NS + st_of(j)] : 0.f;
     else
-      gn[j] = (act && p.dlast) ? __ldg(p.dlast + row * NS + st_of(j)) : 0.f;
+      gn[j] = (act && p.dlast MSS_AND(in_bounds(row * NS + st_of(j), n_bd * NS, kSiteDlast)))
+                  ? __ldg(p.dlast + row * NS + st_of(j)) : 0.f;
     an[j] = 1.f;
     dAacc[j] = make_float2(0.f, 0.f);
   }
@@ -379,13 +403,17 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
       const int gi = t0 / kCkpt + g;  // carry index of the group
       if (act && t0 + g * kGrp < len) {
         if (gi > 0) {
-          if constexpr (kS == 4) {
-            v = *reinterpret_cast<const float4*>(cs);
-          } else {
-            v.x = cs[0];
-            if constexpr (kS > 1) v.y = cs[1];
+          MSS_IF(in_array(cs, p.chunk_states, n_bd * p.n_chunks * NS, kSiteCarry) &&
+                 in_array(cs + kS - 1, p.chunk_states, n_bd * p.n_chunks * NS, kSiteCarry))
+          {
+            if constexpr (kS == 4) {
+              v = *reinterpret_cast<const float4*>(cs);
+            } else {
+              v.x = cs[0];
+              if constexpr (kS > 1) v.y = cs[1];
+            }
           }
-        } else if (p.h0) {
+        } else if (p.h0 MSS_AND(in_bounds(row * NS + NS - 1, n_bd * NS, kSiteH0))) {
           const float* h0 = p.h0 + row * NS;
           v.x = __ldg(h0 + st_of(0));
           if constexpr (kS > 1) v.y = __ldg(h0 + st_of(1));
@@ -428,18 +456,18 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
       // each warp stages its own channel rows, warp 0 the B and C rows
       const size_t wrow = row0 + wc0;
       const int wo = wc0 * kBT;
-      stage_tile_plain(bD + wo, static_cast<const T*>(p.delta), wrow, n_wch, kCPW, L, t0, lane);
-      stage_tile_plain(bU + wo, static_cast<const T*>(p.u), wrow, n_wch, kCPW, L, t0, lane);
-      stage_tile_plain(bY + wo, static_cast<const T*>(p.dout), wrow, n_wch, kCPW, L, t0, lane);
+      stage_tile_plain(bD + wo, static_cast<const T*>(p.delta), wrow, n_wch, kCPW, L, t0, lane, n_rows);
+      stage_tile_plain(bU + wo, static_cast<const T*>(p.u), wrow, n_wch, kCPW, L, t0, lane, n_rows);
+      stage_tile_plain(bY + wo, static_cast<const T*>(p.dout), wrow, n_wch, kCPW, L, t0, lane, n_rows);
       if (has_z) {
-        stage_tile_plain(bZ + wo, static_cast<const T*>(p.z), wrow, n_wch, kCPW, L, t0, lane);
+        stage_tile_plain(bZ + wo, static_cast<const T*>(p.z), wrow, n_wch, kCPW, L, t0, lane, n_rows);
         stage_tile_plain(bP + wo, static_cast<const T*>(p.out_pre), wrow, n_wch, kCPW, L, t0,
-                         lane);
+                         lane, n_rows);
       }
       if (warp == 0) {
         const size_t brow = static_cast<size_t>(b) * NS;
-        stage_tile_plain(&sh.rawB[s][0][0], p.B32, brow, NS, NS, L, t0, lane);
-        stage_tile_plain(&sh.rawC[s][0][0], p.C32, brow, NS, NS, L, t0, lane);
+        stage_tile_plain(&sh.rawB[s][0][0], p.B32, brow, NS, NS, L, t0, lane, n_bc);
+        stage_tile_plain(&sh.rawC[s][0][0], p.C32, brow, NS, NS, L, t0, lane, n_bc);
       }
       __syncwarp();
     }
@@ -693,7 +721,11 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
         const bool b0 = (c & 1) != 0;
         float4 keep = b0 ? dCq[0] : dBq[0];
         add_xor4(keep, b0 ? dBq[0] : dCq[0], 4);
-        if (live) {
+        // (bounds build) the group's first and last step in this batch's NS x L slice
+        MSS_BOUNDS_ONLY(const long long gsl = static_cast<long long>(st_of(0)) * L + t0 + tg;
+                        const long long gsl_end = gsl + (whole ? 3 : min(3, len - 1 - t0 - tg));)
+        if (live MSS_AND(in_bounds(gsl, static_cast<long long>(NS) * L, kSiteDBC) &&
+                         in_bounds(gsl_end, static_cast<long long>(NS) * L, kSiteDBC))) {
           float* gp = acc_row + tg;
           if (whole) {
             if (det) {
@@ -736,7 +768,8 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
       if constexpr (kWarps == 1) {
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
+        if (lane == 0 MSS_AND(in_bounds(t0, L, kSiteTmaStore) &&
+                              in_bounds(rc + kCh - 1, n_bd, kSiteTmaStore))) {
           tma_store_2d(&maps.du, t0, rc, bU);
           tma_store_2d(&maps.dd, t0, rc, bD);
           if (has_z) tma_store_2d(&maps.dz, t0, rc, bZ);
@@ -746,9 +779,9 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
     } else {
       const size_t wrow = row0 + wc0;
       const int wo = wc0 * kBT;
-      unstage_tile_plain(static_cast<T*>(p.du), bU + wo, wrow, n_wch, L, t0, lane);
-      unstage_tile_plain(static_cast<T*>(p.ddelta), bD + wo, wrow, n_wch, L, t0, lane);
-      if (has_z) unstage_tile_plain(static_cast<T*>(p.dz), bZ + wo, wrow, n_wch, L, t0, lane);
+      unstage_tile_plain(static_cast<T*>(p.du), bU + wo, wrow, n_wch, L, t0, lane, n_rows);
+      unstage_tile_plain(static_cast<T*>(p.ddelta), bD + wo, wrow, n_wch, L, t0, lane, n_rows);
+      if (has_z) unstage_tile_plain(static_cast<T*>(p.dz), bZ + wo, wrow, n_wch, L, t0, lane, n_rows);
       __syncwarp();
     }
   }
@@ -774,10 +807,12 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
 #pragma unroll
     for (int j = 0; j < kS; ++j) {
       const int n = st_of(j);
+      MSS_IF(in_bounds(prow * NS + n, n_seg * n_bd * NS, kSiteDARow))
       p.dA_part[prow * NS + n] = dAacc[j].x + dAacc[j].y;
-      if (p.dh0 && seg == 0) p.dh0[row * NS + n] = an[j] * gn[j];
+      if (p.dh0 && seg == 0 MSS_AND(in_bounds(row * NS + n, n_bd * NS, kSiteDh0)))
+        p.dh0[row * NS + n] = an[j] * gn[j];
     }
-    if (q == 0) {
+    if (q == 0 MSS_AND(in_bounds(prow, n_seg * n_bd, kSiteDDRow))) {
       p.dD_part[prow] = dD_acc;
       p.dbias_part[prow] = dbias_acc;
     }
@@ -817,7 +852,10 @@ __global__ void __launch_bounds__(32)
   auto st_of = [&](int j) { return q + kLPC * (j ^ perm); };
 
   int len = L;
-  if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
+  if (p.seq_lens MSS_AND(in_bounds(b, p.batch, kSiteSeqLens)))
+    len = max(0, min(L, p.seq_lens[b]));
+  const long long n_bd = static_cast<long long>(p.batch) * p.dim;
+  const long long n_rows = n_bd * L, n_bc = static_cast<long long>(p.batch) * NS * L;
   const int seg = blockIdx.z + 1;
   const size_t seg_row = row * p.n_seg + seg;
   const int k_begin = seg * p.seg_tiles;
@@ -828,8 +866,11 @@ __global__ void __launch_bounds__(32)
 
   float a2[kS];
 #pragma unroll
-  for (int j = 0; j < kS; ++j) a2[j] = __ldg(p.A + d * NS + st_of(j)) * kLog2e;
-  const float bias = p.delta_bias ? __ldg(p.delta_bias + d) : 0.f;
+  for (int j = 0; j < kS; ++j)
+    a2[j] = MSS_SEL(in_bounds(d * NS + st_of(j), static_cast<long long>(p.dim) * NS, kSiteA),
+                    __ldg(p.A + d * NS + st_of(j)), 0.f) * kLog2e;
+  const float bias =
+      p.delta_bias MSS_AND(in_bounds(d, p.dim, kSiteBias)) ? __ldg(p.delta_bias + d) : 0.f;
 
   constexpr uint32_t kChBytes = kCh * kBT * sizeof(T);
   constexpr uint32_t kNBytes = NS * kBT * sizeof(float);
@@ -882,12 +923,12 @@ __global__ void __launch_bounds__(32)
         return;
       }
     } else {
-      stage_tile_plain(bD, static_cast<const T*>(p.delta), row0, n_ch, kCh, L, t0, lane);
-      stage_tile_plain(bY, static_cast<const T*>(p.dout), row0, n_ch, kCh, L, t0, lane);
+      stage_tile_plain(bD, static_cast<const T*>(p.delta), row0, n_ch, kCh, L, t0, lane, n_rows);
+      stage_tile_plain(bY, static_cast<const T*>(p.dout), row0, n_ch, kCh, L, t0, lane, n_rows);
       if (has_z)
-        stage_tile_plain(bZ, static_cast<const T*>(p.z), row0, n_ch, kCh, L, t0, lane);
+        stage_tile_plain(bZ, static_cast<const T*>(p.z), row0, n_ch, kCh, L, t0, lane, n_rows);
       stage_tile_plain(&sh.rawC[s][0][0], static_cast<const float*>(p.C32),
-                           static_cast<size_t>(b) * NS, NS, NS, L, t0, lane);
+                           static_cast<size_t>(b) * NS, NS, NS, L, t0, lane, n_bc);
       __syncwarp();
     }
 
@@ -958,8 +999,10 @@ __global__ void __launch_bounds__(32)
   }
   if (act) {
 #pragma unroll
-    for (int j = 0; j < kS; ++j) p.seg_G[seg_row * NS + st_of(j)] = G[j];
-    if (q == 0) p.seg_dsum[seg_row] = dsum;
+    for (int j = 0; j < kS; ++j)
+      MSS_IF(in_bounds(seg_row * NS + st_of(j), n_bd * p.n_seg * NS, kSiteSegG))
+      p.seg_G[seg_row * NS + st_of(j)] = G[j];
+    if (q == 0 MSS_AND(in_bounds(seg_row, n_bd * p.n_seg, kSiteSegDsum))) p.seg_dsum[seg_row] = dsum;
   }
 }
 
@@ -1300,5 +1343,7 @@ unsigned int take_bwd_device_error() {
   cudaMemcpyToSymbol(g_bwd_device_error, &zero, sizeof(zero));
   return v;
 }
+
+void take_bwd_bounds(unsigned long long out[4]) { take_oob_record(out); }
 
 }  // namespace mss

@@ -169,6 +169,34 @@ uint32_t mamba_ss_take_device_error(void) {
   return mss::take_fwd_device_error() | mss::take_bwd_device_error();
 }
 
+int32_t mamba_ss_bounds_checked(void) {
+#ifdef MSS_BOUNDS_CHECK
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+uint64_t mamba_ss_take_bounds_violations(int64_t* first) {
+  unsigned long long f[4], b[4];
+  mss::take_fwd_bounds(f);
+  mss::take_bwd_bounds(b);
+  const unsigned long long* rec = f[0] != 0 ? f : b;
+  if (first) {
+    first[0] = static_cast<int64_t>(rec[1]);
+    first[1] = static_cast<int64_t>(rec[2]);
+    first[2] = static_cast<int64_t>(rec[3]);
+  }
+  return f[0] + b[0];
+}
+
+mss_status mamba_ss_bounds_selftest(void) {
+  const cudaError_t e = mss::launch_bounds_selftest(1000);
+  if (e != cudaSuccess)
+    return mss::set_error(MSS_INTERNAL, std::string("bounds self-test: ") + cudaGetErrorString(e));
+  return MSS_OK;
+}
+
 void mamba_ss_set_deterministic(int32_t on) {
   g_deterministic.store(on ? 1 : 0, std::memory_order_relaxed);
 }

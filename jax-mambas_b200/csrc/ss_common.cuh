@@ -405,6 +405,76 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // TMA copies (see mamba_ss_take_device_error()).
 constexpr unsigned int kErrTmaTimeout = 1u;
 
+// ------------------------------------------------------- debug bounds build
+// With MSS_BOUNDS_CHECK defined (the bounds library, libmamba_ss_b200_bounds.so),
+// every plain global access whose index the kernels compute, and the
+// coordinates of every TMA store, is checked against the extent of its array
+// before it is made. An index outside [0, extent) is counted, the first one
+// per compilation unit recorded (site, index, extent) in g_oob, and the
+// access skipped, so that a wrong index shows up as a report on the host
+// (mamba_ss_take_bounds_violations()) instead of a memory fault. Without the
+// flag in_bounds() is the constant true and the checks compile away. Extents
+// are in elements of the array's own type.
+enum BoundsSite : int {
+  kSiteSeqLens = 1, kSiteA, kSiteD, kSiteBias, kSiteH0, kSiteSegIn, kSiteCarry,
+  kSiteOut, kSitePre, kSiteRowIn, kSiteBCIn, kSiteSegEnd, kSiteSegDsum, kSiteLast,
+  kSiteDlast, kSiteSegCarry, kSiteDBC, kSiteDARow, kSiteDDRow, kSiteDh0, kSiteRowOut,
+  kSiteTmaStore, kSiteSegG, kSiteParamOut, kSiteBCOut, kSiteSelfTest = 99
+};
+#ifdef MSS_BOUNDS_CHECK
+// [0] count, [1] site, [2] index, [3] extent of the first violation
+static __device__ unsigned long long g_oob[4];
+#endif
+__device__ __forceinline__ bool in_bounds(long long i, long long n, int site) {
+#ifdef MSS_BOUNDS_CHECK
+  if (i >= 0 && i < n) return true;
+  if (atomicAdd(&g_oob[0], 1ull) == 0ull) {
+    g_oob[1] = static_cast<unsigned long long>(site);
+    g_oob[2] = static_cast<unsigned long long>(i);
+    g_oob[3] = static_cast<unsigned long long>(n);
+  }
+  return false;
+#else
+  (void)i;
+  (void)n;
+  (void)site;
+  return true;
+#endif
+}
+// p lies inside the n elements that start at base
+template <typename T>
+__device__ __forceinline__ bool in_array(const T* p, const T* base, long long n, int site) {
+  return in_bounds(static_cast<long long>(p - base), n, site);
+}
+// The kernels' check sites. Without MSS_BOUNDS_CHECK they expand to nothing
+// (MSS_SEL to its second argument), so that the normal library is compiled
+// from the same text as if no check were written:
+//   MSS_IF(c) stmt;          stmt only if c (bounds build)
+//   cond MSS_AND(c)          adds "&& c" to an existing condition
+//   MSS_SEL(c, a, b)         c ? a : b (bounds build), a (normal build)
+//   MSS_BOUNDS_ONLY(stmts)   statements of the bounds build only
+#ifdef MSS_BOUNDS_CHECK
+#define MSS_IF(c) if (c)
+#define MSS_AND(c) && (c)
+#define MSS_SEL(c, a, b) ((c) ? (a) : (b))
+#define MSS_BOUNDS_ONLY(...) __VA_ARGS__
+#else
+#define MSS_IF(c)
+#define MSS_AND(c)
+#define MSS_SEL(c, a, b) (a)
+#define MSS_BOUNDS_ONLY(...)
+#endif
+// Host side: copy this compilation unit's record into out[4] and clear it
+// (all zero in a build without the checks).
+static inline void take_oob_record(unsigned long long out[4]) {
+  for (int i = 0; i < 4; ++i) out[i] = 0ull;
+#ifdef MSS_BOUNDS_CHECK
+  const unsigned long long zero[4] = {0ull, 0ull, 0ull, 0ull};
+  if (cudaMemcpyFromSymbol(out, g_oob, sizeof(zero)) == cudaSuccess)
+    cudaMemcpyToSymbol(g_oob, zero, sizeof(zero));
+#endif
+}
+
 // ------------------------------------------------------- packed fp32 pairs
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
@@ -465,7 +535,12 @@ __device__ __forceinline__ void flush_part(const float4 (*part)[NS], float* acc_
     hi.x += __shfl_xor_sync(0xffffffffu, hi.x, m);
     hi.y += __shfl_xor_sync(0xffffffffu, hi.y, m);
   }
-  if (h == 0) {
+  // state row o's steps t .. t + 3 (or up to len) of this batch's NS x L slice
+  if (h == 0 MSS_AND(in_bounds(static_cast<long long>(o) * L + t,
+                               static_cast<long long>(NS) * L, kSiteDBC) &&
+                     in_bounds(static_cast<long long>(o) * L + t +
+                                   (whole ? 3 : min(3, len - 1 - t)),
+                               static_cast<long long>(NS) * L, kSiteDBC))) {
     float* gp = acc_b + static_cast<size_t>(o) * L + t;
     if (whole) {
       const float4 v4 = make_float4(lo.x, lo.y, hi.x, hi.y);

@@ -145,7 +145,12 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
   const size_t row = static_cast<size_t>(b) * p.dim + d;
 
   int len = L;
-  if (p.seq_lens) len = max(0, min(L, p.seq_lens[b]));
+  if (p.seq_lens MSS_AND(in_bounds(b, p.batch, kSiteSeqLens)))
+    len = max(0, min(L, p.seq_lens[b]));
+  // extents of the arrays, in elements (bounds build only)
+  MSS_BOUNDS_ONLY(const long long n_bd = static_cast<long long>(p.batch) * p.dim;
+                  const long long n_rows = n_bd * L;
+                  const long long n_bc = static_cast<long long>(p.batch) * NS * L;)
 
   // this CTA's time segment: tiles [k_begin, k_end)
   const int seg = blockIdx.z;
@@ -157,13 +162,15 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
 #pragma unroll
   for (int j = 0; j < kS; ++j) {
     const int n = st_of(j);
-    Av[j] = __ldg(p.A + d * NS + n);
+    Av[j] = MSS_SEL(in_bounds(d * NS + n, static_cast<long long>(p.dim) * NS, kSiteA),
+                    __ldg(p.A + d * NS + n), 0.f);
     a2[j] = Av[j] * kLog2e;
     float h0 = 0.f;
     if (!kEnd && lane_active) {
       if (seg > 0)
-        h0 = p.seg_in[seg_row * NS + n];
-      else if (p.h0)
+        h0 = MSS_SEL(in_bounds(seg_row * NS + n, n_bd * p.n_seg * NS, kSiteSegIn),
+                     p.seg_in[seg_row * NS + n], 0.f);
+      else if (p.h0 MSS_AND(in_bounds(row * NS + n, n_bd * NS, kSiteH0)))
         h0 = __ldg(p.h0 + row * NS + n);
     }
     h[j] = h0;
@@ -215,8 +222,10 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
     const int c = it_c0 + k * kItemChStride;
-    it_bias[k] = (p.delta_bias && c < n_ch) ? __ldg(p.delta_bias + d0 + c) : 0.f;
-    it_D[k] = (p.D && c < n_ch) ? __ldg(p.D + d0 + c) : 0.f;
+    it_bias[k] = (p.delta_bias && c < n_ch MSS_AND(in_bounds(d0 + c, p.dim, kSiteBias)))
+                     ? __ldg(p.delta_bias + d0 + c) : 0.f;
+    it_D[k] = (p.D && c < n_ch MSS_AND(in_bounds(d0 + c, p.dim, kSiteD)))
+                  ? __ldg(p.D + d0 + c) : 0.f;
   }
 
   if (use_tma) {
@@ -279,7 +288,9 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
               const size_t off = static_cast<size_t>(d0 + c) * L + t0 + tt;
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                if (t0 + tt + e < len) {
+                if (t0 + tt + e < len MSS_AND(in_array(dl_b + off + e,
+                                                       static_cast<const T*>(p.delta), n_rows,
+                                                       kSiteRowIn))) {
                   x[e] = Elem<T>::ld(dl_b + off + e);
                   uv[e] = Elem<T>::ld(u_b + off + e);
                 }
@@ -315,7 +326,8 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
             const size_t off = static_cast<size_t>(n) * L + t0 + tt;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              if (t0 + tt + e < len) {
+              if (t0 + tt + e < len MSS_AND(in_array(B_b + off + e, static_cast<const T*>(p.B),
+                                                     n_bc, kSiteBCIn))) {
                 bv[e] = Elem<T>::ld(B_b + off + e);
                 cv[e] = Elem<T>::ld(C_b + off + e);
               }
@@ -438,7 +450,9 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
             }
             // carry after these 4 steps (entries past the valid length are not
             // written: the backward never reads them; none for forward-only calls)
-            if (lane_active && save_carries) {
+            if (lane_active && save_carries
+                    MSS_AND(in_array(cs, p.chunk_states,
+                                     n_bd * p.n_chunks * NS - (kS - 1), kSiteCarry))) {
               if constexpr (kS == 4) {
                 *reinterpret_cast<float4*>(cs) = make_float4(h[0], h[1], h[2], h[3]);
               } else {
@@ -480,8 +494,13 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
             } else {
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                uv[e] = t + e < len ? Elem<T>::ld(u_b + off + e) : 0.f;
-                if (z_b) zv[e] = t + e < L ? Elem<T>::ld(z_b + off + e) : 0.f;
+                uv[e] = t + e < len MSS_AND(in_array(u_b + off + e, static_cast<const T*>(p.u),
+                                                     n_rows, kSiteRowIn))
+                            ? Elem<T>::ld(u_b + off + e) : 0.f;
+                if (z_b)
+                  zv[e] = t + e < L MSS_AND(in_array(z_b + off + e, static_cast<const T*>(p.z),
+                                                     n_rows, kSiteRowIn))
+                              ? Elem<T>::ld(z_b + off + e) : 0.f;
               }
             }
             const float4 y4 = *reinterpret_cast<const float4*>(&sh.ys[c][tt]);
@@ -494,6 +513,10 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
               }
             }
           }
+          MSS_BOUNDS_ONLY(
+              if (!in_array(out_b + off, static_cast<T*>(p.out), n_rows, kSiteOut) ||
+                  !in_array(out_b + off + min(4, L - t) - 1, static_cast<T*>(p.out), n_rows,
+                            kSiteOut)) continue;)
           if (kFull || use_tma) {  // whole, aligned groups: L is a multiple of 4 here
             store4_global(out_b + off, o);
             if (pre_b) store4_global(pre_b + off, pre);
@@ -522,12 +545,17 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
   if constexpr (kEnd) {
     if (lane_active) {
 #pragma unroll
-      for (int j = 0; j < kS; ++j) p.seg_end[seg_row * NS + st_of(j)] = h[j];
-      if (q == 0) p.seg_dsum[seg_row] = dsum;
+      for (int j = 0; j < kS; ++j)
+        MSS_IF(in_bounds(seg_row * NS + st_of(j), n_bd * p.n_seg * NS, kSiteSegEnd))
+        p.seg_end[seg_row * NS + st_of(j)] = h[j];
+      if (q == 0 MSS_AND(in_bounds(seg_row, n_bd * p.n_seg, kSiteSegDsum)))
+        p.seg_dsum[seg_row] = dsum;
     }
   } else if (p.last_state && lane_active && seg == p.n_seg - 1) {
 #pragma unroll
-    for (int j = 0; j < kS; ++j) p.last_state[row * NS + st_of(j)] = h[j];
+    for (int j = 0; j < kS; ++j)
+      MSS_IF(in_bounds(row * NS + st_of(j), n_bd * NS, kSiteLast))
+      p.last_state[row * NS + st_of(j)] = h[j];
   }
 }
 
@@ -721,6 +749,19 @@ unsigned int take_fwd_device_error() {
   if (cudaMemcpyFromSymbol(&v, g_fwd_device_error, sizeof(v)) != cudaSuccess) return ~0u;
   cudaMemcpyToSymbol(g_fwd_device_error, &zero, sizeof(zero));
   return v;
+}
+
+void take_fwd_bounds(unsigned long long out[4]) { take_oob_record(out); }
+
+// One thread checks index n + 7 against extent n without touching memory:
+// the bounds build must count and record it (site kSiteSelfTest).
+__global__ void bounds_selftest_kernel(long long n) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) (void)in_bounds(n + 7, n, kSiteSelfTest);
+}
+
+cudaError_t launch_bounds_selftest(long long n) {
+  bounds_selftest_kernel<<<1, 32>>>(n);
+  return cudaPeekAtLastError();
 }
 
 }  // namespace mss

@@ -81,6 +81,13 @@ mss_status set_error(mss_status code, const std::string& msg);
 unsigned int take_fwd_device_error();
 unsigned int take_bwd_device_error();
 
+// Debug bounds build: copy and clear the forward / backward compilation
+// units' out-of-bounds records ([0] count, [1] site, [2] index, [3] extent;
+// all zero without MSS_BOUNDS_CHECK), and launch the checker's self-test.
+void take_fwd_bounds(unsigned long long out[4]);
+void take_bwd_bounds(unsigned long long out[4]);
+cudaError_t launch_bounds_selftest(long long n);
+
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 

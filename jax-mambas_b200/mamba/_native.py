@@ -99,6 +99,9 @@ SIGNATURES = {
     "mamba_ss_debug_set_wait_polls": (None, [ctypes.c_int64]),
     "mamba_ss_set_deterministic": (None, [_i32]),
     "mamba_ss_deterministic": (_i32, []),
+    "mamba_ss_bounds_checked": (_i32, []),
+    "mamba_ss_take_bounds_violations": (ctypes.c_uint64, [ctypes.POINTER(ctypes.c_int64)]),
+    "mamba_ss_bounds_selftest": (ctypes.c_int, []),
     "mamba_ss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "mamba_ss_fused_bwd_noalloc": (
         ctypes.c_int,
