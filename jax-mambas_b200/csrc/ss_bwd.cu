@@ -13,6 +13,7 @@
 #include <cstddef>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 #include "ss_common.cuh"
 #include "ss_launch.h"
@@ -211,7 +212,10 @@ __device__ void zero_rows(T* base, size_t row0, int n, int L, int from, int to, 
 // spill (3.55 ms); the group loop unrolled by 1 or 4 measured 3.59 / 3.96 ms.
 // kWarps: warps per CTA (TileShared); the CTA's kCh channels are kWarps
 // blocks of kCPW, one per warp.
-template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false, int kWarps = 1>
+// kStd: the fused layer's usual call (softplus on delta, a z gate, dB/dC by
+// atomics), with those three choices compiled in instead of tested per group.
+template <int NS, typename T, bool kZOH, bool kSeg, bool kLPT = false, int kWarps = 1,
+          bool kStd = false>
 __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0)
     ss_bwd_tile_kernel(const BwdParams p, const __grid_constant__ TileMaps maps) {
   using Cfg = TileCfg<NS>;
@@ -266,7 +270,8 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
   const size_t seg_row = row * n_seg + seg;
   const bool use_tma = p.tma_ok != 0;
   const bool tma_store = use_tma && n_ch == kCh;  // whole boxes stay in this batch
-  const bool has_z = p.z != nullptr;
+  const bool has_z = kStd || p.z != nullptr;
+  const bool softplus_on = kStd || p.delta_softplus != 0;
 
   float Av[kS], a2[kS];
 #pragma unroll
@@ -366,7 +371,7 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
                                               reinterpret_cast<uintptr_t>(p.dC_acc)) & 15) == 0;
   // deterministic mode: this warp's column of the partial sums instead of
   // the accumulators, written instead of added
-  const bool det = p.dBC_part != nullptr;
+  const bool det = !kStd && p.dBC_part != nullptr;
   const int col = static_cast<int>(blockIdx.x) * kWarps + warp;
   float* const part_b =
       det ? p.dBC_part + static_cast<size_t>(b * p.n_cols + col) * 2 * NS * L : nullptr;
@@ -472,8 +477,13 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
       __syncwarp();
     }
 
-    // ---- 1. transform: lane (c, q) takes steps [q * kBT / kLPC, ...) of channel c
-    {
+    // ---- 1. transform: lane (c, q) takes steps [q * kBT / kLPC, ...) of channel c.
+    // A full tile (every channel of the CTA live, every step valid, 16-byte
+    // aligned accumulator rows) runs this and the group walk without the
+    // per-element and per-group validity tests.
+    const bool full = n_ch == kCh && t0 + kBT <= len && acc_aligned;
+    auto transform = [&](auto full_t) {
+      constexpr bool kFull = decltype(full_t)::value;
       constexpr int kQ = kBT / 4 / kLPC;
 #pragma unroll
       for (int qq = 0; qq < kQ; ++qq) {
@@ -494,9 +504,9 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
         float dl[4], dy[4], dz[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const bool valid = act && t0 + tt + e < len;
+          const bool valid = kFull || (act && t0 + tt + e < len);
           float xe = xs[e] + bias;
-          if (p.delta_softplus) xe = softplus_f(xe);
+          if (softplus_on) xe = softplus_f(xe);
           float ye = ys[e], ze = 0.f;
           if (has_z) {
             const float sz = sigmoid_f(zs[e]);
@@ -512,6 +522,11 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
         st4s(wY, c, tt, make_float4(dy[0], dy[1], dy[2], dy[3]));
         if (has_z) st4s(bZ, c, tt, make_float4(dz[0], dz[1], dz[2], dz[3]));
       }
+    };
+    if (full) {
+      transform(std::true_type{});
+    } else {
+      transform(std::false_type{});
     }
     if constexpr (kWarps > 1) {
       // the CTA's barrier of the tile: past it every warp is done with
@@ -574,6 +589,8 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
     };
 
     // ---- 3. groups in reverse
+    auto groups = [&](auto full_t) {
+      constexpr bool kFull = decltype(full_t)::value;
 #pragma unroll 2
     for (int g = kNG - 1; g >= 0; --g) {
       const int tg = g * kGrp;
@@ -670,12 +687,12 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
       const int owd = grp_off(rD, kW, g), owu = grp_off(rU, kU, g);
       auto emit = [&](int e, float sa, float sb) {
         const int tl = tg + e;
-        const bool valid = act && t0 + tl < len;
+        const bool valid = kFull || (act && t0 + tl < len);
         const float dlv = rD[owd + e];
         const float dyv = rY[owd + e];
         const float uv = to_f32(rU[owu + e]);
         float gd = kZOH ? sa : fmaf(uv, sb, sa);
-        if (p.delta_softplus) gd *= sigmoid_from_softplus(dlv);
+        if (softplus_on) gd *= sigmoid_from_softplus(dlv);
         const float du = fmaf(Dv, dyv, kZOH ? sb : dlv * sb);
         gd = valid ? gd : 0.f;
         dbias_acc += gd;
@@ -711,8 +728,8 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
       }
 
       // dB and dC of the group: sum the channels, add into the accumulators
-      const bool live = t0 + tg < len;  // warp-uniform
-      const bool whole = t0 + tg + kGrp <= len && acc_aligned;
+      const bool live = kFull || t0 + tg < len;  // warp-uniform
+      const bool whole = kFull || (t0 + tg + kGrp <= len && acc_aligned);
       if constexpr (kShflFlush) {
         // level 2 (channel bit 1): slot 1 to the partner; level 3 (bit 0):
         // lanes with bit 0 clear keep dB, the others dC, of state st_of(0)
@@ -760,6 +777,12 @@ __global__ void __launch_bounds__(32 * kWarps, kLPT ? (kWarps == 1 ? 16 : 7) : 0
         if (live) flush_part<NS>(sh.part, dC_b, L, t0 + tg, len, whole, lane, det);
         __syncwarp();
       }
+    }
+    };
+    if (full) {
+      groups(std::true_type{});
+    } else {
+      groups(std::false_type{});
     }
 
     // ---- 4. the tile's du, ddelta, dz (multi-warp CTAs with TMA stores:
@@ -1129,8 +1152,14 @@ static cudaError_t launch_bwd_main(const BwdParams& p, const TileMaps& maps,
   const size_t smem = offsetof(Sh, barP) + sizeof(uint64_t);
   auto kern = ss_bwd_tile_kernel<NS, T, kZOH, false, false, kWarps>;
   if constexpr (NS == 16 && !kZOH) {
-    if (p.seq_lens != nullptr && p.n_seg == 1 && p.batch <= kLongestFirstMax)
-      kern = ss_bwd_tile_kernel<NS, T, kZOH, false, true, kWarps>;
+    const bool std_call = p.delta_softplus != 0 && p.z != nullptr && p.dBC_part == nullptr;
+    const bool lpt = p.seq_lens != nullptr && p.n_seg == 1 && p.batch <= kLongestFirstMax;
+    if (lpt) {
+      kern = std_call ? ss_bwd_tile_kernel<NS, T, kZOH, false, true, kWarps, true>
+                      : ss_bwd_tile_kernel<NS, T, kZOH, false, true, kWarps>;
+    } else if (std_call && p.n_seg == 1) {
+      kern = ss_bwd_tile_kernel<NS, T, kZOH, false, false, kWarps, true>;
+    }
   }
   if (p.n_seg > 1) kern = ss_bwd_tile_kernel<NS, T, kZOH, true, false, kWarps>;
   cudaError_t e = cudaFuncSetAttribute(
