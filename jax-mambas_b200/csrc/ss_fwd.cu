@@ -78,8 +78,9 @@ struct FwdShared {
   alignas(1024) T rawC[2][kNSP][kTile];
   // fp32 work tiles
   float dlt[kCh][kRow];  // delta_eff
-  float dlu[kCh][kRow];  // delta_eff * u   (ZOH: u)
-  float ys[kCh][kRow];   // sum_n C_t h_t
+  // delta_eff * u (ZOH: u); each 4-step group's entries are overwritten by
+  // y_t = sum_n C_t h_t of those steps once every lane has read them
+  float dlu[kCh][kRow];
   // widened B/C (bf16 I/O only; fp32 I/O reads the swizzled staging)
   float Bs[sizeof(T) == 4 ? 1 : NS][kRow];
   float Cs[sizeof(T) == 4 ? 1 : NS][kRow];
@@ -109,7 +110,11 @@ __device__ __forceinline__ void store4_global(__nv_bfloat16* dst, const float (&
 // a zero state, its final state and sum of delta_eff to seg_end / seg_dsum).
 // kLPT: right-padded batches, grid rows take the sequences longest first
 // (batch_of_row).
-template <int NS, typename T, bool kZOH, bool kEnd, bool kWide, bool kLPT = false>
+// kStd: the fused layer's usual call (softplus on delta, a z gate, the
+// pre-gate output and the carries saved for the backward), with those
+// choices compiled in instead of tested per element or step group.
+template <int NS, typename T, bool kZOH, bool kEnd, bool kWide, bool kLPT = false,
+          bool kStd = false>
 __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     ss_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   using Cfg = FwdCfg<NS, kWide>;
@@ -180,6 +185,9 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
   const size_t bdl = static_cast<size_t>(b) * p.dim * L;
   const T* u_b = static_cast<const T*>(p.u) + bdl;
   const T* dl_b = static_cast<const T*>(p.delta) + bdl;
+  const bool has_z = kStd || p.z != nullptr;
+  const bool has_pre = kStd || p.out_pre != nullptr;
+  const bool softplus_on = kStd || p.delta_softplus != 0;
   const T* z_b = p.z ? static_cast<const T*>(p.z) + bdl : nullptr;
   T* out_b = static_cast<T*>(p.out) + bdl;
   T* pre_b = p.out_pre ? static_cast<T*>(p.out_pre) + bdl : nullptr;
@@ -199,7 +207,7 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
     }
     constexpr uint32_t kChBytes = kCh * kTile * sizeof(T);
     constexpr uint32_t kNBytes = NS * kTile * sizeof(T);
-    const bool with_z = z_b && !kEnd;
+    const bool with_z = has_z && !kEnd;
     mbar_arrive_expect_tx(bar, (with_z ? 3 : 2) * kChBytes + (kEnd ? 1 : 2) * kNBytes);
     const int rc = b * p.dim + d0;  // first channel row
     tma_load_2d(&sh.rawD[s][0][0], &maps.d, t0, rc, bar);
@@ -302,7 +310,7 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
           for (int e = 0; e < 4; ++e) {
             const bool valid = kFull || (c < n_ch && t0 + tt + e < len);
             const float xe = x[e] + it_bias[k];
-            const float de = p.delta_softplus ? softplus_f(xe) : xe;
+            const float de = softplus_on ? softplus_f(xe) : xe;
             dv[e] = valid ? de : 0.f;
             du[e] = valid ? (kZOH ? uv[e] : de * uv[e]) : 0.f;
           }
@@ -371,7 +379,7 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
                     "rawC follows rawB");
       const float* const rdl = &sh.dlt[cl][0];
       const float* const rdu = &sh.dlu[cl][0];
-      const bool save_carries = p.chunk_states != nullptr;
+      const bool save_carries = kStd || p.chunk_states != nullptr;
       float* cs = p.chunk_states + carry_offset(b, t0 / kCkpt, p.n_chunks, p.dim, d, NS) + q * kS;
       const size_t cs_step = static_cast<size_t>(p.dim) * NS;  // next carry index
       auto scan = [&](auto full_t) {
@@ -435,18 +443,18 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
               const float sx = hi1 ? k0 : k1;
               float kk = hi1 ? k1 : k0;
               kk += __shfl_xor_sync(0xffffffffu, sx, 1);
-              sh.ys[cl][tt + q] = kk;  // step tt + q
+              sh.dlu[cl][tt + q] = kk;  // step tt + q
             } else if constexpr (kLPC == 2) {
               const bool hi = (q & 1) != 0;
               const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
               float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
               k0 += __shfl_xor_sync(0xffffffffu, s0, 1);
               k1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-              sh.ys[cl][tt + 2 * q] = k0;
-              sh.ys[cl][tt + 2 * q + 1] = k1;
+              sh.dlu[cl][tt + 2 * q] = k0;
+              sh.dlu[cl][tt + 2 * q + 1] = k1;
             } else {
 #pragma unroll
-              for (int e = 0; e < 4; ++e) sh.ys[cl][tt + e] = yp[e];
+              for (int e = 0; e < 4; ++e) sh.dlu[cl][tt + e] = yp[e];
             }
             // carry after these 4 steps (entries past the valid length are not
             // written: the backward never reads them; none for forward-only calls)
@@ -490,26 +498,26 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
             float zv[4], uv[4];
             if (kFull || use_tma) {
               load4_smem(&sh.rawU[s][c][tt], uv);
-              if (z_b) load4_smem(&sh.rawZ[s][c][tt], zv);
+              if (has_z) load4_smem(&sh.rawZ[s][c][tt], zv);
             } else {
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 uv[e] = t + e < len MSS_AND(in_array(u_b + off + e, static_cast<const T*>(p.u),
                                                      n_rows, kSiteRowIn))
                             ? Elem<T>::ld(u_b + off + e) : 0.f;
-                if (z_b)
+                if (has_z)
                   zv[e] = t + e < L MSS_AND(in_array(z_b + off + e, static_cast<const T*>(p.z),
                                                      n_rows, kSiteRowIn))
                               ? Elem<T>::ld(z_b + off + e) : 0.f;
               }
             }
-            const float4 y4 = *reinterpret_cast<const float4*>(&sh.ys[c][tt]);
+            const float4 y4 = *reinterpret_cast<const float4*>(&sh.dlu[c][tt]);
             const float ys4[4] = {y4.x, y4.y, y4.z, y4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (kFull || t + e < len) {
                 pre[e] = fmaf(it_D[k], uv[e], ys4[e]);
-                o[e] = z_b ? pre[e] * silu_f(zv[e]) : pre[e];
+                o[e] = has_z ? pre[e] * silu_f(zv[e]) : pre[e];
               }
             }
           }
@@ -519,13 +527,13 @@ __global__ void __launch_bounds__(FwdCfg<NS, kWide>::kThreads)
                             kSiteOut)) continue;)
           if (kFull || use_tma) {  // whole, aligned groups: L is a multiple of 4 here
             store4_global(out_b + off, o);
-            if (pre_b) store4_global(pre_b + off, pre);
+            if (has_pre) store4_global(pre_b + off, pre);
           } else {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (t + e < L) {
                 Elem<T>::st(out_b + off + e, o[e]);
-                if (pre_b) Elem<T>::st(pre_b + off + e, pre[e]);
+                if (has_pre) Elem<T>::st(pre_b + off + e, pre[e]);
               }
             }
           }
@@ -599,8 +607,13 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps, bool wi
     if (wide) {  // unsegmented only
       using CfgW = FwdCfg<NS, true>;
       const size_t smem_w = sizeof(FwdShared<NS, T, true>);
-      auto kern_w = longest_first(p) ? ss_fwd_kernel<NS, T, kZOH, false, true, true>
-                                     : ss_fwd_kernel<NS, T, kZOH, false, true>;
+      const bool std_call = p.delta_softplus != 0 && p.z != nullptr && p.out_pre != nullptr &&
+                            p.chunk_states != nullptr;
+      auto kern_w = longest_first(p)
+                        ? (std_call ? ss_fwd_kernel<NS, T, kZOH, false, true, true, true>
+                                    : ss_fwd_kernel<NS, T, kZOH, false, true, true>)
+                        : (std_call ? ss_fwd_kernel<NS, T, kZOH, false, true, false, true>
+                                    : ss_fwd_kernel<NS, T, kZOH, false, true>);
       cudaError_t e = cudaFuncSetAttribute(
           kern_w, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_w));
       if (e != cudaSuccess) return e;
