@@ -1159,9 +1159,14 @@ static cudaError_t launch_bwd_main(const BwdParams& p, const TileMaps& maps,
                       : ss_bwd_tile_kernel<NS, T, kZOH, false, true, kWarps>;
     } else if (std_call && p.n_seg == 1) {
       kern = ss_bwd_tile_kernel<NS, T, kZOH, false, false, kWarps, true>;
+    } else if (std_call) {
+      kern = ss_bwd_tile_kernel<NS, T, kZOH, true, false, kWarps, true>;
+    } else if (p.n_seg > 1) {
+      kern = ss_bwd_tile_kernel<NS, T, kZOH, true, false, kWarps>;
     }
+  } else {
+    if (p.n_seg > 1) kern = ss_bwd_tile_kernel<NS, T, kZOH, true, false, kWarps>;
   }
-  if (p.n_seg > 1) kern = ss_bwd_tile_kernel<NS, T, kZOH, true, false, kWarps>;
   cudaError_t e = cudaFuncSetAttribute(
       kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;

@@ -626,7 +626,13 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const FwdMaps& maps, bool wi
   const size_t smem = sizeof(FwdShared<NS, T>);
   auto kern = ss_fwd_kernel<NS, T, kZOH, false, false>;
   if constexpr (NS == 16) {
-    if (longest_first(p)) kern = ss_fwd_kernel<NS, T, kZOH, false, false, true>;
+    const bool std_call = p.delta_softplus != 0 && p.z != nullptr && p.out_pre != nullptr &&
+                          p.chunk_states != nullptr;
+    if (longest_first(p)) {
+      kern = ss_fwd_kernel<NS, T, kZOH, false, false, true>;
+    } else if (std_call) {
+      kern = ss_fwd_kernel<NS, T, kZOH, false, false, false, true>;
+    }
   }
   auto kern_end = ss_fwd_kernel<NS, T, kZOH, true, false>;
   cudaError_t e = cudaFuncSetAttribute(
