@@ -290,11 +290,14 @@ class ScanCase:
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream(self.dev)
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
-        if self.world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        # the clock sampler (rank 0 only) comes up before the barrier: started
+        # after it, its start-up delayed rank 0's first launch, and the other
+        # ranks' clocks then counted their wait for rank 0 at the first exchange
         ctx = sampler if sampler is not None else _Null()
         with ctx:
+            if self.world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
             t0 = torch.cuda.Event(enable_timing=True)
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record(stream)
